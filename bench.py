@@ -1,0 +1,383 @@
+"""Decode-attention benchmark: us per decode step and effective KV TB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One JSON line on rank 0. A "step" is one decode step of one layer over the
+workload's KV cache (the kernel plus the split merge), with L2 flushed before
+every step (a write of 3 x L2), as the reference times it
+(runtime/kvf_host.h:302-330). The payload is 2 * rows * (row bytes + 4 * groups)
+(runtime/kvf_driver.cu:51) over the stored tokens; value = payload of all
+ranks / max-over-ranks step time, in TB/s.
+
+  value   device time of the step, inputs resident in HBM, CUDA events on the
+          launching stream
+  e2e     the same step through the public API (kvf_b200_decode) with the query
+          copied in from pinned host memory and the output copied back, inside
+          the timed region; the KV cache itself stays resident, as a decode cache
+          does
+  --impl reference
+          the reference's own CPU implementation of the path,
+          kvf::reference_attention (runtime/kvf_host.h:202-234, compiled
+          unmodified into oracle/_ref), on the host cores, over disjoint
+          (sequence, KV head) slices in parallel threads
+
+At N > 1 GPUs the headline workload (not sharded by the reference) runs as N
+independent replicas (weak scaling, no collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--workload", default=None)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--splits", type=int, default=0, help="override the split count")
+    p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (s)")
+    return p.parse_args()
+
+
+def measured_peaks() -> dict:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """NVML SM clock and throttle reasons, sampled every 2 ms in a thread."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000002: "applications_clocks_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: no clock record
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def record(self) -> dict:
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- reference arm
+def reference_step_fn(w, threads: int, sample_seqs=None):
+    """One decode step of the reference's CPU path on the same workload:
+    kvf::reference_attention over each (sequence, KV head) slice of the
+    dequantised cache, slices spread over `threads` threads."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    import torch
+
+    from kvforge_b200 import workloads
+    from oracle import oracle as O
+
+    import dataclasses
+
+    B = w.B if sample_seqs is None else min(w.B, sample_seqs)
+    qd, Kd, Vd, seq_lens = workloads.generate(dataclasses.replace(w, B=B), "cpu")
+    q = qd.numpy()
+    K = Kd.numpy()
+    V = Vd.numpy()
+    _, _, kd = O.quantize(w.fmt, w.d, w.group, K.reshape(-1, w.d))
+    _, _, vd = O.quantize(w.fmt, w.d, w.group, V.reshape(-1, w.d))
+    kd = kd.reshape(K.shape)
+    vd = vd.reshape(V.shape)
+    g = w.H // w.Hkv
+    scale = O.scale_f32(w.d)
+    slices = []
+    for b in range(B):
+        nb = w.n if seq_lens is None else int(seq_lens[b])
+        for h in range(w.Hkv):
+            slices.append((np.ascontiguousarray(q[b : b + 1, h * g : (h + 1) * g]),
+                           np.ascontiguousarray(kd[b : b + 1, h : h + 1, :nb]),
+                           np.ascontiguousarray(vd[b : b + 1, h : h + 1, :nb])))
+    ref_lib = O.Ref.available()
+    fn = O.Ref.attention if ref_lib else (lambda a, b_, c, s: O.attention(a, b_, c, s, threads=1))
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+    tokens = sum(s[1].shape[2] for s in slices)
+    payload = 2 * tokens * (w.d * (16 if w.fmt == 0 else 8 if w.fmt == 1 else 4) // 8 +
+                            (0 if w.fmt == 0 else 4 * (w.d // w.group)))
+
+    def step():
+        list(pool.map(lambda s: fn(s[0], s[1], s[2], scale), slices))
+
+    return step, payload, ("reference" if ref_lib else "port"), B
+
+
+def run_reference_arm(args, w, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    # A bounded sample: at most 8 sequences of the workload per step.
+    step, payload, kind, nseq = reference_step_fn(w, threads, sample_seqs=8)
+    for _ in range(max(1, min(args.warmup, 2))):
+        step()
+    steps = args.steps
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    steps = max(1, min(steps, int(60.0 / max(one, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    tbs = payload / dt / 1e12
+    sample = f"{nseq} of {w.B} sequences per step, all KV heads, dequantised fp32 K/V"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "us_per_step": dt * 1e6,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic", "config": w.config() | {"sample_sequences": nseq},
+        "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": tbs, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(w, budget_s: float) -> dict:
+    threads = os.cpu_count() or 1
+    step, payload, kind, nseq = reference_step_fn(w, threads, sample_seqs=8)
+    step()
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        step()
+        reps += 1
+        if time.perf_counter() - t0 > min(budget_s, 30.0) or reps >= 20:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": payload / dt / 1e12, "unit": "TB/s", "cores": threads, "kind": kind,
+            "us_per_step": dt * 1e6,
+            "sample": f"{nseq} of {w.B} sequences, {reps} steps, kvf::reference_attention (fp64) "
+                      f"over (sequence, KV head) slices on {threads} threads"}
+
+
+METRIC = "decode-attn effective KV TB/s (payload bytes / us per step)"
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    from kvforge_b200 import workloads
+
+    wname = args.workload or workloads.HEADLINE
+    w = workloads.CONFIGS[wname]
+    if args.impl == "reference":
+        run_reference_arm(args, w, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    import ctypes
+
+    import torch
+
+    from kvforge_b200 import api
+    from kvforge_b200._native import check, lib
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    qd, Kd, Vd, seq_lens = workloads.generate(w, dev, seed=w.seed + rank)
+    cache = api.KVCache.from_logical(Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens)
+    del Kd, Vd
+    torch.cuda.empty_cache()
+    splits = args.splits or api.suggest_splits(cache, w.H)
+    ws = api.Workspace.allocate(w.B, w.H, w.d, splits, dev)
+    out = torch.empty_like(qd)
+    payload = cache.payload_bytes()
+    args_blk = api.make_args(qd, cache, out, ws)
+    stream = torch.cuda.current_stream(dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    L = lib()
+    g = w.H // w.Hkv
+
+    def launch():
+        check("kvf_b200_decode", L.kvf_b200_decode(ctypes.byref(args_blk), w.fmt, w.d, g, w.place.order,
+                                                   int(w.place.paged), sptr))
+
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    flush = torch.empty(max(96 << 20, 3 * l2), dtype=torch.uint8, device=dev)
+
+    for i in range(args.warmup):
+        flush.fill_(i & 0xFF)
+        launch()
+    torch.cuda.synchronize()
+
+    # ---- device-timed steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            launch()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    times_ms = [a.elapsed_time(b) for a, b in ev]
+    ms = statistics.mean(times_ms)
+    ms_med = statistics.median(times_ms)
+    ms_all = max_over_ranks(ms, world)
+    errs = api.device_errors()
+
+    # ---- end to end through the public API, host buffers
+    q_host = qd.cpu().pin_memory()
+    out_host = torch.empty_like(out, device="cpu").pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.warmup):
+        flush.fill_(i & 0xFF)
+        qd.copy_(q_host, non_blocking=True)
+        api.decode(qd, cache, out=out, workspace=ws)
+        out_host.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        ev2[i][0].record(stream)
+        qd.copy_(q_host, non_blocking=True)
+        api.decode(qd, cache, out=out, workspace=ws)
+        out_host.copy_(out, non_blocking=True)
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev2), world)
+
+    total_payload = payload * world
+    value = total_payload / (ms_all * 1e-3) / 1e12
+    peaks = measured_peaks()
+    achieved_gbs = payload / (ms * 1e-3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / f"{wname}.traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+    launches_per_step = 2 if splits > 1 else 1
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_all, "us_per_step": ms_all * 1e3,
+            "us_per_step_median": ms_med * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": {0: "f16 KV", 1: "int8 KV", 2: "int4 KV"}[w.fmt] + ", fp32 accumulate",
+            "data": "synthetic (seeded N(0,1) on device)",
+            "config": w.config() | {"splits": splits, "payload_bytes_per_gpu": payload,
+                                    "l2": "flushed before every step (3 x L2 write)",
+                                    "parallelism": "replicas" if world > 1 else "1 GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_source": peaks["source"] + " copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                         "timed": "decode kernel + split merge per step"},
+            "e2e": {"value": total_payload / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s", "us_per_step": e2e_ms * 1e3,
+                    "h2d_bytes_per_step": qd.numel() * 4, "d2h_bytes_per_step": out.numel() * 4},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.record(),
+            "device_errors": errs,
+        }
+        if world == 1 and args.cpu_sample_s > 0:
+            line["cpu_baseline"] = cpu_baseline(w, args.cpu_sample_s)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+/* kvforge_b200.h - C ABI of the B200 (sm_100a) decode-attention kernels.
+ *
+ * One decode step of one attention layer: every query head attends to the
+ * n cached tokens of its sequence, over a KV cache stored as f16, int8:G or
+ * int4:G (asymmetric per-group scale and zero point), head-major or
+ * token-major, contiguous or paged. Results are written to `out`.
+ *
+ * This header is plain C (plain pointers and sizes, no C++ or torch types) so
+ * it can be bound from ctypes, cgo or JNI. The C++ drop-in for the reference's
+ * `kvf::launch<>` / `kvf::Args` (runtime/kvf_kernels.cuh) is kvf_kernels.cuh in
+ * this directory; it forwards to the functions below.
+ *
+ * Error behaviour follows the reference launcher (runtime/kvf_kernels.cuh:309-320):
+ * every entry point returns a cudaError_t, never throws, never synchronises
+ * and never exits. Launches are stream-ordered; the library holds no state
+ * between calls apart from cached driver entry points.
+ */
+#ifndef KVFORGE_B200_H
+#define KVFORGE_B200_H
+
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage formats and placements: same values as kvf::Fmt / kvf::Ord
+ * (runtime/kvf_kernels.cuh:26-27). */
+enum { KVF_FMT_F16 = 0, KVF_FMT_INT8 = 1, KVF_FMT_INT4 = 2 };
+enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
+
+/* Kernel argument block. Field order and types are those of kvf::Args
+ * (runtime/kvf_kernels.cuh:29-46), so a pointer to a reference kvf::Args is a
+ * valid kvf_args pointer. Fields after scale_log2 are additions; callers that
+ * zero-initialise the struct (`kvf::Args a{}`) get the reference behaviour.
+ *
+ *   q            [B][H][D] fp32
+ *   k, v         cache payload; row r holds one token's D channels of one KV
+ *                head: f16 2*D bytes, int8 D bytes, int4 D/2 bytes (column c in
+ *                byte c/2, odd columns in the high nibble)
+ *   k_meta,v_meta [rows][D/group] words, each (scale | zero << 16) as fp16
+ *                (a __half2 with .x = scale); quantized formats only
+ *   block_table  [B][max_blocks] page ids, paged layouts only
+ *   out          [B][H][D] fp32
+ *   part_o       [B][H][splits][D] fp32 workspace, used when splits > 1
+ *   part_ml      [B][H][splits][2] fp32 workspace (running max in log2 units,
+ *                running sum), used when splits > 1
+ *   splits       partitions of each sequence's tokens (>= 1)
+ *   warps        reference tuning knob; accepted and ignored on sm_100a
+ *   group_shift  log2(quantization group), quantized formats
+ *   block_shift  log2(tokens per page), paged layouts
+ *   scale_log2   softmax scale * log2(e)
+ *   seq_lens     [B] tokens of each sequence (each <= n); NULL = all n.
+ */
+typedef struct kvf_args {
+  const float *q;
+  const unsigned char *k;
+  const unsigned char *v;
+  const void *k_meta;
+  const void *v_meta;
+  const int *block_table;
+  float *out;
+  float *part_o;
+  float *part_ml;
+  int B, H, Hkv, n;
+  int splits;
+  int warps;
+  int group_shift;
+  int block_shift;
+  int max_blocks;
+  float scale_log2;
+  /* ---- additions (zero = reference behaviour) ---- */
+  const int *seq_lens;
+} kvf_args;
+
+/* One decode step: the sm_100a counterpart of
+ * kvf::launch<FMT, D, G, U, ORD, PAGED>(a, st) (runtime/kvf_kernels.cuh:309-320),
+ * i.e. decode_partial (:124-285) plus, when a->splits > 1, the log-sum-exp
+ * merge decode_merge (:288-306).
+ *   fmt    KVF_FMT_*;  d  64 or 128;  ord  KVF_ORD_*;  paged  0/1
+ *   g      query heads per KV head the caller packed (1, or H/Hkv). The
+ *          sm_100a kernels always pack every query head of a KV head into one
+ *          block, so 1 and H/Hkv give the same result; other values are
+ *          rejected with cudaErrorInvalidValue.
+ * Returns cudaSuccess, cudaErrorInvalidValue (bad shape, format, group, page
+ * size or null pointer), cudaErrorMisalignedAddress (k or v not 16-byte
+ * aligned, meta not 4-byte aligned), or the launch error. */
+cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                            cudaStream_t stream);
+
+/* The split merge alone (decode_merge<D>, runtime/kvf_kernels.cuh:288-306):
+ * out[b][h] = sum_s part_o[s] * 2^(m_s - M) / sum_s l_s * 2^(m_s - M). */
+cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream);
+
+/* Launch by variant id, e.g. "int8_tm_p_g4_u2_d128": the registry lookup plus
+ * call of bench/sweep.cu:180-184 (id format of src/codegen.cpp:59-65,
+ * fmt_{hm,tm}_{c,p}_g{1,2,4,8}_u{2,4}_d{64,128}). Unknown ids return
+ * cudaErrorInvalidDeviceFunction. */
+cudaError_t kvf_b200_launch_variant(const char *variant_id, const kvf_args *a,
+                                    cudaStream_t stream);
+
+/* Number of variant ids this library registers, and the i-th id (NULL when i
+ * is out of range). Mirrors kvf_register_all (gen/kvf_dispatch.cu). */
+int kvf_b200_variant_count(void);
+const char *kvf_b200_variant_name(int i);
+
+/* Split count the sm_100a kernels run best with for this shape: the
+ * B200 counterpart of the planner's `splits` choice (src/plan.cpp:25-35).
+ * n is the longest sequence. Always >= 1. */
+int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group, int paged,
+                            int block_tokens);
+
+/* Writes a one-line description of the launch kvf_b200_decode would make
+ * (grid, block, stages, tokens per stage, shared memory) into buf. Returns
+ * the same status kvf_b200_decode would return for these arguments, without
+ * launching anything. */
+cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged, char *buf,
+                              int buf_len);
+
+/* Device-side error word of the current device, then cleared. Bit 0: a
+ * shared-memory barrier wait in a decode kernel ran out of time (the kernel
+ * abandoned the step and its output is not valid). 0 = no error. This call
+ * synchronises with the device. */
+unsigned kvf_b200_device_errors(void);
+
+/* Quantizes `rows` logical rows of d fp32 channels (device memory) into the
+ * cache format: the device counterpart of kvf::quantize
+ * (runtime/kvf_host.h:72-120), bit-exact with it. `data` receives
+ * rows * row_bytes bytes; for int8/int4 `meta` receives rows * (d / group)
+ * words (scale | zero << 16, fp16). f16 ignores group and meta. */
+cudaError_t kvf_b200_quantize(int fmt, int d, int group, const float *x, long long rows,
+                              unsigned char *data, void *meta, cudaStream_t stream);
+
+/* Library version string. */
+const char *kvf_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVFORGE_B200_H */

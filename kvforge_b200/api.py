@@ -1,0 +1,223 @@
+"""Torch-facing host API over the C ABI.
+
+`KVCache.from_logical` plays the role of the reference's quantize +
+upload_cache (runtime/kvf_host.h:72-120, :149-195): quantize logical rows on
+the device, then place them in the chosen layout. `decode` is one decode step
+through kvf_b200_decode (the counterpart of kvf::launch<>,
+runtime/kvf_kernels.cuh:309-320); `make_args` fills the argument block as
+make_args does (runtime/kvf_host.h:273-293).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import layout
+from ._native import FMT_F16, FMT_INT4, FMT_INT8, KvfArgs, check, lib
+from .layout import Placement
+
+LOG2E = 1.4426950408889634
+
+
+def row_bytes(fmt: int, d: int) -> int:
+    return 2 * d if fmt == FMT_F16 else d if fmt == FMT_INT8 else d // 2
+
+
+def groups_per_row(fmt: int, d: int, group: int) -> int:
+    return 0 if fmt == FMT_F16 else d // group
+
+
+def scale_log2(d: int) -> float:
+    """(1/sqrt(D)) * log2(e) in fp32, as make_args computes it (kvf_host.h:292)."""
+    s = np.float32(1.0) / np.sqrt(np.float32(d))
+    return float(np.float32(s) * np.float32(LOG2E))
+
+
+def _stream(stream) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def quantize(x: torch.Tensor, fmt: int, group: int = 0, stream=None):
+    """Quantize rows of x (float32 [..., D], CUDA) on the device.
+
+    Returns (data uint8 [rows, row_bytes], meta int32 [rows, D/group] or None).
+    Bit-exact with kvf::quantize (runtime/kvf_host.h:72-120)."""
+    if not x.is_cuda or x.dtype != torch.float32:
+        raise ValueError("quantize expects a float32 CUDA tensor")
+    d = x.shape[-1]
+    x2 = x.reshape(-1, d).contiguous()
+    rows = x2.shape[0]
+    data = torch.empty((rows, row_bytes(fmt, d)), dtype=torch.uint8, device=x.device)
+    gpr = groups_per_row(fmt, d, group)
+    meta = torch.empty((rows, gpr), dtype=torch.int32, device=x.device) if gpr else None
+    check(
+        "kvf_b200_quantize",
+        lib().kvf_b200_quantize(fmt, d, group, x2.data_ptr(), rows, data.data_ptr(),
+                                meta.data_ptr() if meta is not None else None, _stream(stream)),
+    )
+    return data, meta
+
+
+@dataclass
+class KVCache:
+    """A KV cache resident on one device, in one format and placement."""
+
+    fmt: int
+    d: int
+    group: int
+    place: Placement
+    B: int
+    Hkv: int
+    n: int
+    k: torch.Tensor                      # uint8 [rows_alloc, row_bytes]
+    v: torch.Tensor
+    k_meta: Optional[torch.Tensor]       # int32 [rows_alloc, D/group]
+    v_meta: Optional[torch.Tensor]
+    block_table: Optional[torch.Tensor]  # int32 [B, max_blocks]
+    max_blocks: int
+    seq_lens: Optional[torch.Tensor]     # int32 [B]
+
+    @property
+    def gpr(self) -> int:
+        return groups_per_row(self.fmt, self.d, self.group)
+
+    def payload_bytes(self) -> int:
+        """KV payload of one decode step: 2 * valid rows * (row bytes + 4 * groups),
+        the formula of runtime/kvf_driver.cu:51 over the stored tokens."""
+        tokens = int(self.seq_lens.sum().item()) if self.seq_lens is not None else self.B * self.n
+        rows = tokens * self.Hkv
+        return 2 * rows * (row_bytes(self.fmt, self.d) + 4 * self.gpr)
+
+    @classmethod
+    def from_logical(cls, K: torch.Tensor, V: torch.Tensor, *, fmt: int, group: int = 0,
+                     place: Placement, seq_lens=None, table_seed: int = 18) -> "KVCache":
+        """Build a cache from logical float32 K, V [B][Hkv][n][D] on a CUDA device."""
+        B, Hkv, n, d = K.shape
+        dev = K.device
+        kq, km = quantize(K, fmt, group)
+        vq, vm = quantize(V, fmt, group)
+        table = None
+        max_blocks = 0
+        pages = 0
+        sl = None if seq_lens is None else np.asarray(seq_lens, dtype=np.int32)
+        if place.paged:
+            table, max_blocks, pages = layout.page_table(B, n, place.block_tokens, table_seed, sl)
+        nrows = layout.rows_alloc(B, Hkv, n, place, pages)
+        phys = layout.physical_rows(B, Hkv, n, place, table, sl)
+        keep = np.nonzero(phys >= 0)[0]
+        src = torch.from_numpy(keep).to(dev)
+        dst = torch.from_numpy(phys[keep]).to(dev)
+
+        def place_rows(x):
+            if x is None:
+                return None
+            out = torch.zeros((nrows, x.shape[1]), dtype=x.dtype, device=dev)
+            out.index_copy_(0, dst, x.index_select(0, src))
+            return out
+
+        cache = cls(
+            fmt=fmt, d=d, group=group, place=place, B=B, Hkv=Hkv, n=n,
+            k=place_rows(kq), v=place_rows(vq), k_meta=place_rows(km), v_meta=place_rows(vm),
+            block_table=torch.from_numpy(table).to(dev) if table is not None else None,
+            max_blocks=max_blocks,
+            seq_lens=torch.from_numpy(sl).to(dev) if sl is not None else None,
+        )
+        return cache
+
+
+@dataclass
+class Workspace:
+    """Split partials: part_o [B][H][splits][D] and part_ml [B][H][splits][2]."""
+
+    splits: int
+    part_o: Optional[torch.Tensor]
+    part_ml: Optional[torch.Tensor]
+
+    @classmethod
+    def allocate(cls, B: int, H: int, d: int, splits: int, device) -> "Workspace":
+        if splits <= 1:
+            return cls(1, None, None)
+        return cls(
+            splits,
+            torch.empty((B, H, splits, d), dtype=torch.float32, device=device),
+            torch.empty((B, H, splits, 2), dtype=torch.float32, device=device),
+        )
+
+
+def suggest_splits(cache: KVCache, H: int) -> int:
+    bt = cache.place.block_tokens if cache.place.paged else 0
+    return int(lib().kvf_b200_suggest_splits(cache.B, H, cache.Hkv, cache.n, cache.fmt, cache.d,
+                                             cache.group, int(cache.place.paged), bt))
+
+
+def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace) -> KvfArgs:
+    B, H, d = q.shape
+    a = KvfArgs()
+    a.q = q.data_ptr()
+    a.k = cache.k.data_ptr()
+    a.v = cache.v.data_ptr()
+    a.k_meta = cache.k_meta.data_ptr() if cache.k_meta is not None else None
+    a.v_meta = cache.v_meta.data_ptr() if cache.v_meta is not None else None
+    a.block_table = cache.block_table.data_ptr() if cache.block_table is not None else None
+    a.out = out.data_ptr()
+    a.part_o = ws.part_o.data_ptr() if ws.part_o is not None else None
+    a.part_ml = ws.part_ml.data_ptr() if ws.part_ml is not None else None
+    a.B, a.H, a.Hkv, a.n = B, H, cache.Hkv, cache.n
+    a.splits = ws.splits
+    a.warps = 4
+    a.group_shift = int(round(math.log2(cache.group))) if cache.fmt != FMT_F16 else 0
+    a.block_shift = int(round(math.log2(cache.place.block_tokens))) if cache.place.paged else 0
+    a.max_blocks = cache.max_blocks
+    a.scale_log2 = scale_log2(d)
+    a.seq_lens = cache.seq_lens.data_ptr() if cache.seq_lens is not None else None
+    return a
+
+
+def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = None,
+           splits: Optional[int] = None, workspace: Optional[Workspace] = None, stream=None,
+           g: int = 1) -> torch.Tensor:
+    """One decode step: out[b][h] = softmax(q k^T * scale) v over the cache.
+
+    q: float32 [B][H][D] on the cache's device. Returns out (float32 [B][H][D])."""
+    if q.dtype != torch.float32 or not q.is_contiguous():
+        raise ValueError("q must be a contiguous float32 tensor [B][H][D]")
+    B, H, d = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    if workspace is None:
+        s = splits if splits is not None else suggest_splits(cache, H)
+        workspace = Workspace.allocate(B, H, d, s, q.device)
+    a = make_args(q, cache, out, workspace)
+    check(
+        "kvf_b200_decode",
+        lib().kvf_b200_decode(ctypes.byref(a), cache.fmt, d, g, cache.place.order,
+                              int(cache.place.paged), _stream(stream)),
+    )
+    return out
+
+
+def describe(q: torch.Tensor, cache: KVCache, workspace: Workspace) -> str:
+    out = torch.empty(0)
+    B, H, d = q.shape
+    a = make_args(q, cache, q, workspace)
+    buf = ctypes.create_string_buffer(512)
+    check("kvf_b200_describe",
+          lib().kvf_b200_describe(ctypes.byref(a), cache.fmt, d, cache.place.order,
+                                  int(cache.place.paged), buf, 512))
+    del out
+    return buf.value.decode()
+
+
+def device_errors() -> int:
+    return int(lib().kvf_b200_device_errors())
+
+
+__all__ = ["KVCache", "Workspace", "decode", "quantize", "suggest_splits", "make_args", "describe",
+           "device_errors", "row_bytes", "groups_per_row", "scale_log2", "FMT_F16", "FMT_INT8", "FMT_INT4"]

@@ -1,0 +1,419 @@
+// decode.cu - host side of the sm_100a decode-attention kernels: argument
+// checks, launch planning (heads per block, stage depth, split chunking), TMA
+// tensor-map encoding and the C-ABI entry points declared in kvforge_b200.h.
+//
+// The reference launcher this replaces is kvf::launch<> in
+// runtime/kvf_kernels.cuh:309-320 (grid (splits, G>1 ? Hkv : H, B), the partial
+// kernel, then decode_merge when splits > 1).
+#include "kvforge_b200.h"
+
+#include "decode_kernel.cuh"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+namespace kvfb {
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+int ilog2(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return s;
+}
+
+struct Shape {
+  int fmt, d, ord, paged, bt, gpr;
+};
+
+// Validates the arguments the way the reference's preconditions state them
+// (runtime/kvf_kernels.cuh:131-132, src/ir.cpp:122-133, src/format.cpp:90-102,
+// src/layout.cpp:62-78).
+cudaError_t check_args(const kvf_args *a, int fmt, int d, int g, int ord, int paged, Shape &sh) {
+  if (!a) return cudaErrorInvalidValue;
+  if (fmt < 0 || fmt > 2 || (d != 64 && d != 128) || (ord != 0 && ord != 1)) return cudaErrorInvalidValue;
+  if (a->B < 0 || a->H <= 0 || a->Hkv <= 0 || a->H % a->Hkv || a->n < 0 || a->splits < 1)
+    return cudaErrorInvalidValue;
+  const int gq = a->H / a->Hkv;
+  if (gq > 8) return cudaErrorInvalidValue;
+  if (g != 1 && g != gq) return cudaErrorInvalidValue;
+  sh.fmt = fmt;
+  sh.d = d;
+  sh.ord = ord;
+  sh.paged = paged ? 1 : 0;
+  sh.gpr = 0;
+  sh.bt = 0;
+  if (fmt != 0) {
+    if (a->group_shift < 5 || a->group_shift > 7) return cudaErrorInvalidValue;
+    const int group = 1 << a->group_shift;
+    if (group > d || (fmt == 1 && group < 64)) return cudaErrorInvalidValue;
+    sh.gpr = d / group;
+    if (!a->k_meta || !a->v_meta) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a->k_meta) | reinterpret_cast<uintptr_t>(a->v_meta)) &
+        (uintptr_t)(4 * sh.gpr - 1))
+      return cudaErrorMisalignedAddress;
+  }
+  if (sh.paged) {
+    if (a->block_shift < 4 || a->block_shift > 7) return cudaErrorInvalidValue;
+    sh.bt = 1 << a->block_shift;
+    if (!a->block_table || a->max_blocks < (a->n + sh.bt - 1) / sh.bt) return cudaErrorInvalidValue;
+  }
+  if (a->B == 0 || a->H == 0) return cudaSuccess;
+  if (!a->q || !a->k || !a->v || !a->out) return cudaErrorInvalidValue;
+  if (a->splits > 1 && (!a->part_o || !a->part_ml)) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a->k) | reinterpret_cast<uintptr_t>(a->v)) & 15u)
+    return cudaErrorMisalignedAddress;
+  if ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->out)) & 3u)
+    return cudaErrorMisalignedAddress;
+  return cudaSuccess;
+}
+
+bool group_ok(int fmt, int d, int group) {
+  if (fmt == 0) return true;
+  if (group != 32 && group != 64 && group != 128) return false;
+  return group <= d && !(fmt == 1 && group < 64);
+}
+
+int heads_per_block(int Hkv, int fmt, int d) {
+  // Four KV heads (consumer warps) per block keep a stage near 32 KB and let
+  // two blocks share an SM, each with its own barriers, so one block's
+  // dependent softmax chain overlaps the other's.
+  (void)fmt;
+  (void)d;
+  for (int h = 4; h > 1; h >>= 1)
+    if (Hkv % h == 0) return h;
+  return 1;
+}
+
+template <int FMT, int D, int GPR, int NT> struct K {
+  static void *fn() { return reinterpret_cast<void *>(&decode_kernel<FMT, D, GPR, NT>); }
+};
+
+// Kernel for (fmt, d, gpr, nt); nullptr for an unsupported combination.
+void *kernel_for(int fmt, int d, int gpr, int nt) {
+#define KVFB_CASE(F, DD, G, N)                                                     \
+  if (fmt == F && d == DD && gpr == G && nt == N) return K<F, DD, G, N>::fn();
+#define KVFB_NT(F, DD, G) KVFB_CASE(F, DD, G, 1) KVFB_CASE(F, DD, G, 2)
+  KVFB_NT(0, 128, 0) KVFB_NT(0, 64, 0)
+  KVFB_NT(1, 128, 1) KVFB_NT(1, 128, 2) KVFB_NT(1, 64, 1)
+  KVFB_NT(2, 128, 1) KVFB_NT(2, 128, 2) KVFB_NT(2, 128, 4) KVFB_NT(2, 64, 1) KVFB_NT(2, 64, 2)
+#undef KVFB_NT
+#undef KVFB_CASE
+  return nullptr;
+}
+
+struct KernelInfo {
+  int regs = 0;
+  int static_smem = 0;
+  bool ok = false;
+};
+
+KernelInfo info_for(void *fn) {
+  static std::mutex mu;
+  static void *keys[64];
+  static KernelInfo vals[64];
+  static int count = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < count; ++i)
+    if (keys[i] == fn) return vals[i];
+  KernelInfo ki;
+  cudaFuncAttributes at;
+  if (cudaFuncGetAttributes(&at, fn) == cudaSuccess) {
+    ki.regs = at.numRegs;
+    ki.static_smem = (int)at.sharedSizeBytes;
+    ki.ok = true;
+  } else {
+    cudaGetLastError();
+  }
+  if (count < 64) {
+    keys[count] = fn;
+    vals[count++] = ki;
+  }
+  return ki;
+}
+
+constexpr int kSmemPerSM = 228 * 1024;
+constexpr int kSmemPerBlockMax = 227 * 1024;
+constexpr int kReservedPerBlock = 1024;
+
+struct Launch {
+  Plan p;
+  void *fn = nullptr;
+  int threads = 0;
+  int blocks = 0;
+  int occupancy = 0;
+};
+
+cudaError_t plan_launch(const kvf_args *a, const Shape &sh, Launch &L) {
+  Plan &p = L.p;
+  std::memset(&p, 0, sizeof(p));
+  const int gq = a->H / a->Hkv;
+  const int nt = gq <= 4 ? 1 : 2;
+  L.fn = kernel_for(sh.fmt, sh.d, sh.gpr, nt);
+  if (!L.fn) return cudaErrorInvalidValue;
+  p.gq = gq;
+  p.gpr = sh.gpr;
+  p.hh = heads_per_block(a->Hkv, sh.fmt, sh.d);
+  p.hg = a->Hkv / p.hh;
+  const int rb = row_bytes(sh.fmt, sh.d);
+  p.rb = rb;
+  p.tb = 16 * stage_mtiles(sh.fmt, sh.d);
+  p.paged = sh.paged;
+  p.tm = sh.ord;
+  p.bt_shift = sh.paged ? ilog2(sh.bt) : 0;
+  p.tbox = sh.paged ? std::min(p.tb, sh.bt) : p.tb;
+  p.tbox_shift = ilog2(p.tbox);
+  p.npg = p.tb / p.tbox;
+  p.boxx = std::min(rb, 128);
+  p.nxb = rb / p.boxx;
+  p.swz = p.boxx == 128 ? 0x70u : p.boxx == 64 ? 0x30u : 0x10u;
+  p.box_bytes = (uint32_t)(p.boxx * p.tbox * p.hh);
+  p.kv_bytes = (uint32_t)(p.tb * p.hh * rb);
+  p.meta_bytes = (uint32_t)(p.tb * p.hh * sh.gpr * 4);
+  p.tx_bytes = 2u * p.kv_bytes;
+  const uint32_t meta_al = (p.meta_bytes + 127u) & ~127u;
+  p.stage_bytes = (2u * p.kv_bytes + 2u * meta_al + 1023u) & ~1023u;
+  const int ng = sh.gpr > 0 ? sh.gpr : 1;
+  p.pscr_warp = (uint32_t)(ng * nt * 384);
+  L.threads = (p.hh + 1) * 32;
+
+  const KernelInfo ki = info_for(L.fn);
+  if (!ki.ok) return cudaErrorInvalidDeviceFunction;
+  // Blocks per SM the registers allow (at most 2), then as many stages as the
+  // shared memory of that many blocks holds.
+  const int regs_per_block = ((ki.regs + 7) / 8 * 8) * L.threads;
+  int occ = std::max(1, std::min(2, 65536 / std::max(1, regs_per_block)));
+  const uint32_t fixed = 1024u + 16u * 8u + p.pscr_warp * p.hh + (uint32_t)ki.static_smem;
+  int stages = 0;
+  for (; occ >= 1; --occ) {
+    const int budget = std::min(kSmemPerBlockMax, kSmemPerSM / occ - kReservedPerBlock) - (int)fixed;
+    stages = std::min(8, budget / (int)p.stage_bytes);
+    if (stages >= 2) break;
+  }
+  if (stages < 2) return cudaErrorInvalidValue;
+  L.occupancy = occ;
+  p.stages = stages;
+  p.off_bars = (uint32_t)stages * p.stage_bytes;
+  p.off_pscr = p.off_bars + 16u * (uint32_t)stages;
+  p.off_pscr = (p.off_pscr + 127u) & ~127u;
+  p.smem_total = 1024u + p.off_pscr + p.pscr_warp * (uint32_t)p.hh;
+
+  p.splits = a->splits;
+  p.final_out = a->splits == 1;
+  const int per = (a->n + a->splits - 1) / std::max(1, a->splits);
+  p.chunk = std::max(p.tb, (per + p.tb - 1) / p.tb * p.tb);
+  if (sh.paged && sh.bt > p.tb) p.chunk = (p.chunk + sh.bt - 1) / sh.bt * sh.bt;
+  L.blocks = a->B * p.hg * a->splits;
+  return cudaSuccess;
+}
+
+cudaError_t encode_maps(const kvf_args *a, const Shape &sh, const Plan &p, CUtensorMap &tk,
+                        CUtensorMap &tv) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t rb = (cuuint64_t)p.rb;
+  cuuint64_t dims[4], strides[3];
+  dims[0] = rb;
+  dims[2] = (cuuint64_t)a->Hkv;
+  if (sh.paged) {
+    const cuuint64_t bt = (cuuint64_t)sh.bt;
+    const cuuint64_t page = bt * a->Hkv * rb;
+    dims[1] = bt;
+    dims[3] = std::min<cuuint64_t>((1ull << 31) - 1, ((1ull << 40) - 1) / page);
+    strides[0] = sh.ord ? a->Hkv * rb : rb;
+    strides[1] = sh.ord ? rb : bt * rb;
+    strides[2] = page;
+  } else {
+    const cuuint64_t n = (cuuint64_t)std::max(a->n, 1);
+    dims[1] = n;
+    dims[3] = (cuuint64_t)std::max(a->B, 1);
+    strides[0] = sh.ord ? a->Hkv * rb : rb;
+    strides[1] = sh.ord ? rb : n * rb;
+    strides[2] = n * a->Hkv * rb;
+  }
+  const cuuint32_t box[4] = {(cuuint32_t)p.boxx, (cuuint32_t)p.tbox, (cuuint32_t)p.hh, 1u};
+  const cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+  const CUtensorMapSwizzle swz = p.boxx == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : p.boxx == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = enc(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<unsigned char *>(a->k), dims,
+                   strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  r = enc(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<unsigned char *>(a->v), dims, strides,
+          box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)a->H, (unsigned)a->B, (unsigned)((d + 31) / 32));
+  cfg.blockDim = dim3(kMergeWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const kvf_args args = *a;
+  return cudaLaunchKernelEx(&cfg, merge_kernel, args, d);
+}
+
+} // namespace
+} // namespace kvfb
+
+using namespace kvfb;
+
+extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                                       cudaStream_t stream) {
+  Shape sh;
+  cudaError_t e = check_args(a, fmt, d, g, ord, paged, sh);
+  if (e != cudaSuccess) return e;
+  if (a->B == 0) return cudaSuccess;
+  Launch L;
+  e = plan_launch(a, sh, L);
+  if (e != cudaSuccess) return e;
+  CUtensorMap tk, tv;
+  e = encode_maps(a, sh, L.p, tk, tv);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
+  if (e != cudaSuccess) return e;
+  const kvf_args args = *a;
+  const Plan plan = L.p;
+  void *params[4] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv};
+  e = cudaLaunchKernel(L.fn, dim3((unsigned)L.blocks), dim3((unsigned)L.threads), params,
+                       L.p.smem_total, stream);
+  if (e != cudaSuccess) return e;
+  if (!L.p.final_out) e = launch_merge(a, d, stream, true);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+extern "C" cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream) {
+  if (!a || (d != 64 && d != 128) || a->splits < 1 || a->H <= 0 || a->B < 0) return cudaErrorInvalidValue;
+  if (a->B == 0) return cudaSuccess;
+  if (!a->part_o || !a->part_ml || !a->out) return cudaErrorInvalidValue;
+  const cudaError_t e = launch_merge(a, d, stream, false);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged,
+                                         char *buf, int buf_len) {
+  Shape sh;
+  cudaError_t e = check_args(a, fmt, d, 1, ord, paged, sh);
+  if (e != cudaSuccess) return e;
+  Launch L;
+  e = plan_launch(a, sh, L);
+  if (e != cudaSuccess) return e;
+  if (buf && buf_len > 0) {
+    const KernelInfo ki = info_for(L.fn);
+    std::snprintf(buf, (size_t)buf_len,
+                  "grid=%d block=%d heads/block=%d tokens/stage=%d stages=%d stage_bytes=%u "
+                  "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d",
+                  L.blocks, L.threads, L.p.hh, L.p.tb, L.p.stages, L.p.stage_bytes, L.p.smem_total,
+                  L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out);
+  }
+  return cudaSuccess;
+}
+
+extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group,
+                                       int paged, int block_tokens) {
+  if (B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || n <= 0 || (d != 64 && d != 128) || fmt < 0 || fmt > 2)
+    return 1;
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+  }
+  cudaGetLastError();
+  const int hh = heads_per_block(Hkv, fmt, d);
+  const int units = B * (Hkv / hh);
+  const int tb = 16 * stage_mtiles(fmt, d);
+  int gran = tb;
+  if (paged && block_tokens > tb) gran = block_tokens;
+  // Blocks per SM from the launch plan (registers and shared memory); 1 when
+  // the kernel cannot be inspected (no device).
+  int occ = 1;
+  {
+    kvf_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.B = B;
+    a.H = H;
+    a.Hkv = Hkv;
+    a.n = n;
+    a.splits = 1;
+    a.group_shift = fmt ? ilog2(std::max(group, 1)) : 0;
+    a.block_shift = paged ? ilog2(std::max(block_tokens, 1)) : 0;
+    Shape sh;
+    sh.fmt = fmt;
+    sh.d = d;
+    sh.ord = 0;
+    sh.paged = paged ? 1 : 0;
+    sh.bt = paged ? block_tokens : 0;
+    sh.gpr = fmt ? d / std::max(group, 1) : 0;
+    Launch L;
+    if (group_ok(fmt, d, group) && H / Hkv <= 8 && plan_launch(&a, sh, L) == cudaSuccess) occ = L.occupancy;
+    cudaGetLastError();
+  }
+  const int slots = sms * occ;
+  const int smax = std::max(1, std::min(1024, (n + gran - 1) / gran));
+  // Pick the split count whose last wave is fullest; prefer fewer splits
+  // (less merge traffic) among near-equal choices, and at least two stages
+  // of work per block unless the sequence is short.
+  int best = 1;
+  double best_score = -1;
+  for (int s = 1; s <= smax; ++s) {
+    const int chunk = ((n + s - 1) / s + gran - 1) / gran * gran;
+    const int used = (n + chunk - 1) / chunk;  // non-empty splits
+    if (used < s) continue;
+    const double waves = (double)units * s / slots;
+    const double eff = waves / std::ceil(waves);
+    const double score = eff - 0.0005 * s - (chunk < 2 * tb && s > 1 ? 0.5 : 0.0);
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
+}
+
+extern "C" unsigned kvf_b200_device_errors(void) {
+  unsigned v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kvfb_error, sizeof(v)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0xFFFFFFFFu;
+  }
+  if (v) cudaMemcpyToSymbol(g_kvfb_error, &zero, sizeof(zero));
+  return v;
+}
+
+extern "C" const char *kvf_b200_version(void) { return "kvforge_b200 0.1 (sm_100a)"; }

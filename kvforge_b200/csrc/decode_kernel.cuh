@@ -1,0 +1,926 @@
+// decode_kernel.cuh - the sm_100a split-KV decode-attention kernel.
+//
+// Counterpart of decode_partial<FMT,D,G,U,ORD,PAGED,FINAL> in the reference
+// (runtime/kvf_kernels.cuh:124-285): one block owns a chunk of one sequence's
+// tokens for `hh` KV heads and all of their query heads, streams the chunk's
+// K/V rows once, and produces either the normalised output (one split) or an
+// unnormalised partial plus (max, sum) in log2 units for the split merge.
+//
+// Structure (B200-first, not a translation of the reference's SIMT loop):
+//
+//  * Producer warp. Lane 0 moves each stage's K and V tiles with tiled TMA
+//    (cp.async.bulk.tensor, 4-D tensor maps that express all four placements:
+//    head/token major x contiguous/paged) into a ring of shared-memory stages
+//    guarded by full/empty mbarriers. The tiles land swizzled (128/64/32-byte
+//    swizzle matching the row size) so the ldmatrix reads below are free of
+//    bank conflicts. Per-row quantization metadata (4-16 bytes per row) is too
+//    small for TMA boxes and is fetched by all 32 lanes with cp.async, whose
+//    completion is counted on the same full barrier.
+//
+//  * One consumer warp per KV head. Scores and the value product run on the
+//    tensor cores with mma.sync m16n8k16 (f16 in, fp32 accumulate), with the
+//    cached tokens as the M dimension:
+//        S^T[16 tokens x 8] = K[16 x D]   * Q^T[D x 8]
+//        O^T[16 dims   x 8] = V^T[16 x 16] * P^T[16 tokens x 8]
+//    The 8 columns are (query head, part) pairs: every fp32 query is split into
+//    fp16 hi + lo parts (q = hi + lo to ~2^-22), and so is every probability,
+//    so the products carry fp32-level accuracy although the tensor-core inputs
+//    are fp16. Integer codes (0..255, 0..15) and fp16 K/V are exact in fp16.
+//    Packed G <= 4 query heads fill one 8-column tile, G <= 8 two.
+//
+//  * Quantized rows are dequantised algebraically as the reference does
+//    (runtime/kvf_kernels.cuh:211,237-240): codes go to fp16 with the
+//    0x6400 magic-exponent trick (exact), each quantization group accumulates
+//    its own dot product, and
+//        s   = sum_g scale_g * dot_g + zero_g * sum(q in g)
+//        acc = sum_t (p_t * scale_t,g) * code_t + sum_t p_t * zero_t,g
+//    where the second term of acc is a rank-1 correction kept in fp32.
+//
+//  * Online softmax in the log2 domain with one rescale per stage.
+#pragma once
+
+#include "ptx.cuh"
+#include "kvforge_b200.h"
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <type_traits>
+
+namespace kvfb {
+
+// Per-launch constants computed by the host launcher (decode.cu) and shared by
+// both sides. All byte offsets are relative to the 1024-aligned dynamic
+// shared-memory base.
+struct Plan {
+  int gq;          // query heads per KV head (<= 8)
+  int gpr;         // quantization groups per row (0 for f16)
+  int hh;          // KV heads per block (one consumer warp each)
+  int hg;          // head groups: Hkv / hh
+  int tb;          // tokens per stage (multiple of 16)
+  int tbox;        // tokens per TMA box (tb, or the page size when smaller)
+  int tbox_shift;  // log2(tbox)
+  int npg;         // boxes along tokens per stage: tb / tbox
+  int nxb;         // boxes along the row: row_bytes / boxx
+  int boxx;        // inner box bytes (<= 128)
+  int rb;          // row bytes
+  int stages;      // ring depth
+  int chunk;       // tokens per split (multiple of tb)
+  int splits;      // splits per sequence
+  int paged;       // page addressing
+  int tm;          // token-major rows (else head-major)
+  int bt_shift;    // log2(tokens per page)
+  int final_out;   // 1: write normalised out; 0: write partials
+  uint32_t swz;    // swizzle mask for the K/V tiles (0x70, 0x30, 0x10)
+  uint32_t box_bytes;   // one TMA box
+  uint32_t kv_bytes;    // K (or V) bytes in one stage
+  uint32_t meta_bytes;  // K (or V) metadata bytes in one stage
+  uint32_t stage_bytes; // one stage, 1024-aligned
+  uint32_t tx_bytes;    // TMA bytes expected per stage (K + V)
+  uint32_t off_bars;    // full[stages], empty[stages]
+  uint32_t off_pscr;    // P^T scratch, pscr_warp bytes per consumer warp
+  uint32_t pscr_warp;
+  uint32_t smem_total;
+};
+
+__device__ unsigned g_kvfb_error;
+enum : unsigned { KVFB_ERR_TIMEOUT = 1u };
+
+// (scale, zero) of an fp16 half2 metadata word.
+__device__ __forceinline__ float2 meta_sz(uint32_t w) { return ptx::unpack_f16x2(w); }
+
+// Integer codes go to the tensor cores centred: int8 code - 128 in [-128, 127],
+// int4 code - 8 in [-8, 7], exact in fp16. The dequantised value is then
+// x = scale * (code - c) + (zero + c * scale), so the code term and the zero
+// term are both small and their sum does not cancel (with raw codes and the
+// group minimum as zero point both terms are several times the result).
+constexpr float kCentre8 = 128.f, kCentre4 = 8.f;
+
+// int8 codes: 4 bytes -> two f16x2 words of centred codes (fp16 1024 + code,
+// minus 1152).
+__device__ __forceinline__ uint32_t u8pair(uint32_t r, uint32_t sel) {
+  return ptx::hsub2_u32(ptx::prmt(r, 0x64646464u, sel), 0x64806480u);
+}
+// int4 codes: nibble pairs (bits 0-3, 16-19) / (bits 4-7, 20-23) -> f16x2.
+__device__ __forceinline__ uint32_t u4lo(uint32_t x) {
+  // (1024 + n) - 1032 = n - 8
+  return ptx::hsub2_u32(ptx::lop3_and_or(x, 0x000F000Fu, 0x64006400u), 0x64086408u);
+}
+__device__ __forceinline__ uint32_t u4hi(uint32_t x) {
+  // (1024 + 16 n) / 16 - 72 = n - 8, all exact in fp16.
+  return ptx::hfma2_u32(ptx::lop3_and_or(x, 0x00F000F0u, 0x64006400u), 0x2C002C00u, 0xD480D480u);
+}
+
+__device__ __forceinline__ void stsm_x2_t(uint32_t addr, uint32_t r0, uint32_t r1) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x2.trans.shared.b16 [%0], {%1, %2};" ::"r"(addr),
+               "r"(r0), "r"(r1)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr));
+}
+
+// fp32 -> (hi, lo) fp16 pair packed as one word, hi in bits 0-15.
+__device__ __forceinline__ uint32_t split_hi_lo(float x) {
+  const __half h = __float2half_rn(x);
+  const float r = x - __half2float(h);
+  return ptx::pack_f16x2(__half2float(h), r);
+}
+
+// Element (column d) of one query row used by a B fragment.
+template <int FMT>
+__device__ __forceinline__ int q_dim(int ks, int c, int j) {
+  // j in 0..3 enumerates b0.lo, b0.hi, b1.lo, b1.hi of k-step ks.
+  if (FMT == 0) return 16 * ks + ((j & 2) ? 8 : 0) + 2 * c + (j & 1);
+  if (FMT == 1) return 16 * ks + 4 * c + j;
+  // int4: two k-steps per 32-column chunk; pairs (0,4) (1,5) | (2,6) (3,7).
+  const int ch = ks >> 1, sub = ks & 1;
+  const int off = (j & 1) ? 4 : 0;
+  const int base = (j & 2) ? 1 : 0;
+  return 32 * ch + 8 * c + 2 * sub + base + off;
+}
+
+// Output column of row r (0..15) of value d-tile md.
+template <int FMT>
+__device__ __forceinline__ int v_dim(int md, int r) {
+  if (FMT == 0) return 16 * md + r;
+  if (FMT == 1) return r < 8 ? 16 * md + 2 * r : 16 * md + 2 * (r - 8) + 1;
+  const int ch = md >> 1, pi = md & 1;
+  return r < 8 ? 32 * ch + 4 * r + 2 * pi : 32 * ch + 4 * (r - 8) + 2 * pi + 1;
+}
+
+// First column of k-step ks (the group it belongs to).
+template <int FMT> __host__ __device__ constexpr int k_dim0(int ks) {
+  return FMT == 2 ? 32 * (ks >> 1) : 16 * ks;
+}
+// First column of value d-tile md.
+template <int FMT> __host__ __device__ constexpr int v_dim0(int md) {
+  return FMT == 2 ? 32 * (md >> 1) : 16 * md;
+}
+
+// Row bytes and 16-token m-tiles per stage, fixed per (format, head dim):
+// one stage moves about 4 KB of K (and of V) per KV head, in up to four
+// independent m-tiles per warp (instruction-level parallelism for the
+// consumer's dependent ldmatrix -> MMA -> softmax chain).
+__host__ __device__ constexpr int row_bytes(int fmt, int d) {
+  return fmt == 0 ? 2 * d : fmt == 1 ? d : d / 2;
+}
+__host__ __device__ constexpr int stage_mtiles(int fmt, int d) {
+  return row_bytes(fmt, d) >= 256 ? 1 : row_bytes(fmt, d) >= 128 ? 2 : 4;
+}
+
+// Waits on an mbarrier phase, giving up when the block has been told to abort
+// or the wait runs out of time; the result is uniform across the warp.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+  bool ok = true;
+  if (!ptx::mbar_try_wait(bar, parity)) {
+    const uint64_t t0 = ptx::globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+      if (ptx::mbar_try_wait(bar, parity)) break;
+      if ((it & 63u) == 0) {
+        if (*abort_flag || ptx::globaltimer_ns() - t0 > 2000000000ull) {
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+// 2^e as a float, for e in [-126, 127].
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// Exponent that brings a positive magnitude m into [2^(top-1), 2^top):
+// top - ceil(log2(m)), or `top` when m is zero.
+__device__ __forceinline__ int norm_exp(float m, int top) {
+  const uint32_t u = __float_as_uint(m);
+  if (m <= 0.f) return top;
+  int e = (int)((u >> 23) & 0xFFu) - 127;
+  if (u & 0x7FFFFFu) e += 1;
+  return top - e;
+}
+
+template <int FMT, int D, int GPR, int NT>
+// At most 4 KV heads (4 consumer warps + 1 producer warp) per block, two
+// blocks per SM.
+__global__ void __launch_bounds__(160, 2)
+decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMap tmk,
+              const __grid_constant__ CUtensorMap tmv) {
+  constexpr int RB = row_bytes(FMT, D);
+  constexpr int NCH = RB / 16;          // 16-byte chunks per row
+  constexpr int KSTEPS = D / 16;        // MMA k-steps per row
+  constexpr int MD = D / 16;            // value d-tiles
+  constexpr int MT = stage_mtiles(FMT, D);
+  constexpr int TB = 16 * MT;           // tokens per stage
+  constexpr int NG = GPR > 0 ? GPR : 1; // accumulator groups
+  constexpr int BOXX = RB < 128 ? RB : 128;
+  constexpr int CPB = BOXX / 16;        // chunks per box row
+  constexpr uint32_t SWZ = BOXX == 128 ? 0x70u : BOXX == 64 ? 0x30u : 0x10u;
+  static_assert(D == 64 || D == 128, "head dimension");
+  static_assert(NT == 1 || NT == 2, "column tiles");
+  static_assert(NCH % 2 == 0 && CPB % 2 == 0, "ldmatrix.x4 covers two chunks of one box");
+
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const uint32_t bar_full = sbase + p.off_bars;
+  const uint32_t bar_empty = bar_full + 8u * p.stages;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work item: (sequence b, head group hgi, split), split fastest so that a
+  // sequence's blocks run together.
+  const int split = blockIdx.x % p.splits;
+  const int rest = blockIdx.x / p.splits;
+  const int hgi = rest % p.hg;
+  const int b = rest / p.hg;
+  int nb = a.n;
+  if (a.seq_lens) nb = min(max(a.seq_lens[b], 0), a.n);
+  const int t0 = split * p.chunk;
+  const int t1 = min(nb, t0 + p.chunk);
+  const int ntiles = t1 > t0 ? (t1 - t0 + TB - 1) / TB : 0;
+  const int tbs = p.tbox_shift;
+
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < p.stages; ++s) {
+      ptx::mbar_init(bar_full + 8u * s, GPR > 0 ? 33u : 1u);
+      ptx::mbar_init(bar_empty + 8u * s, (uint32_t)p.hh);
+    }
+    ptx::fence_barrier_init();
+  }
+  __syncthreads();
+  // The merge kernel (if any) may be scheduled now; it waits for this grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == p.hh) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tmk);
+      ptx::prefetch_tmap(&tmv);
+    }
+    const uint64_t pol = ptx::policy_evict_first();
+    const int bmask = (1 << p.bt_shift) - 1;
+    const int nblk_valid = p.paged ? min(a.max_blocks, (nb + bmask) >> p.bt_shift) : 0;
+    const long long tab0 = (long long)b * a.max_blocks;
+    // Page ids of a 32-block window, one per lane, and of the next window.
+    int win = p.paged ? (t0 >> p.bt_shift) : 0;
+    int pg_cur = 0, pg_nxt = 0;
+    if (p.paged) {
+      if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
+      if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
+    }
+    const int h0 = hgi * p.hh;
+    const uint32_t *kmeta = reinterpret_cast<const uint32_t *>(a.k_meta);
+    const uint32_t *vmeta = reinterpret_cast<const uint32_t *>(a.v_meta);
+    bool ok = true;
+    int issued = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % p.stages;
+      if (i >= p.stages && !warp_wait(bar_empty + 8u * s, ((i / p.stages) - 1) & 1, &s_abort)) {
+        ok = false;
+        break;
+      }
+      const int tt = t0 + i * TB;
+      const uint32_t sk = sbase + s * p.stage_bytes;
+      const uint32_t sv = sk + p.kv_bytes;
+      // Page of each token box of this stage (paged; at most MT boxes).
+      int pages[MT];
+#pragma unroll
+      for (int j = 0; j < MT; ++j) {
+        pages[j] = 0;
+        if (p.paged && j < p.npg) {
+          const int blk = (tt + (j << tbs)) >> p.bt_shift;
+          while (blk >= win + 32) {
+            win += 32;
+            pg_cur = pg_nxt;
+            pg_nxt = (win + 32 + lane < nblk_valid) ? __ldg(a.block_table + tab0 + win + 32 + lane)
+                                                     : 0;
+          }
+          pages[j] = __shfl_sync(0xffffffffu, pg_cur, blk - win);
+        }
+      }
+      if (lane == 0) {
+        ptx::mbar_arrive_expect_tx(bar_full + 8u * s, p.tx_bytes);
+#pragma unroll
+        for (int j = 0; j < MT; ++j) {
+          if (j < p.npg) {
+            const int tok = tt + (j << tbs);
+            const int c1 = p.paged ? (tok & bmask) : tok;
+            const int c3 = p.paged ? pages[j] : b;
+#pragma unroll
+            for (int xb = 0; xb < RB / BOXX; ++xb) {
+              const uint32_t off = (uint32_t)(xb * p.npg + j) * p.box_bytes;
+              ptx::tma_g2s_4d(sk + off, &tmk, xb * BOXX, c1, h0, c3, bar_full + 8u * s, pol);
+              ptx::tma_g2s_4d(sv + off, &tmv, xb * BOXX, c1, h0, c3, bar_full + 8u * s, pol);
+            }
+          }
+        }
+      }
+      if (GPR > 0) {
+        // Metadata rows (hh heads x TB tokens) of the tokens inside the chunk.
+        const uint32_t smk = sv + p.kv_bytes;
+        const uint32_t smv = smk + p.meta_bytes;
+        for (int r = lane; r < p.hh * TB; r += 32) {
+          const int hl = r / TB, t = r - hl * TB;
+          const int tok = tt + t;
+          if (tok >= t1) continue;
+          const int h = h0 + hl;
+          long long row;
+          if (p.paged) {
+            const int j = t >> tbs;
+            int pg = pages[0];
+#pragma unroll
+            for (int jj = 1; jj < MT; ++jj)
+              if (jj == j) pg = pages[jj];
+            const int tl = tok & bmask;
+            const long long base = ((long long)pg * a.Hkv) << p.bt_shift;
+            row = p.tm ? base + (long long)tl * a.Hkv + h : base + ((long long)h << p.bt_shift) + tl;
+          } else {
+            row = p.tm ? ((long long)b * a.n + tok) * a.Hkv + h : ((long long)b * a.Hkv + h) * a.n + tok;
+          }
+          const uint32_t dst = (uint32_t)(r * GPR * 4);
+          if (GPR == 1) {
+            ptx::cp_async_4(smk + dst, kmeta + row);
+            ptx::cp_async_4(smv + dst, vmeta + row);
+          } else if (GPR == 2) {
+            ptx::cp_async_8(smk + dst, kmeta + row * 2);
+            ptx::cp_async_8(smv + dst, vmeta + row * 2);
+          } else {
+            ptx::cp_async_16(smk + dst, kmeta + row * 4);
+            ptx::cp_async_16(smv + dst, vmeta + row * 4);
+          }
+        }
+        ptx::cp_async_arrive(bar_full + 8u * s);
+      }
+      issued = i + 1;
+      if (s_abort) break;
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+      s_abort = 1;
+    }
+    // Never leave with copies in flight: wait (bounded) for the last stages.
+    for (int i = max(0, issued - p.stages); i < issued; ++i) {
+      const int s = i % p.stages;
+      volatile int never = 0;
+      if (!warp_wait(bar_full + 8u * s, (i / p.stages) & 1, &never) && lane == 0)
+        atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumer
+  const int h = hgi * p.hh + warp;  // KV head of this warp
+  const int g8 = lane >> 2;         // fragment row group
+  const int c4 = lane & 3;          // thread in group
+  const float *qbase = a.q + ((long long)b * a.H + (long long)h * p.gq) * D;
+  constexpr float CENTRE = FMT == 1 ? kCentre8 : kCentre4;
+
+  // Q^T fragments: column n = g8 holds (query head nt*4 + g8/2, part g8&1).
+  // Each head is pre-scaled by a power of two 2^eq (max |q| in [2^13, 2^14))
+  // before the fp16 hi/lo split, so the lo part never drops into fp16's
+  // subnormal range; scores are scaled back by 2^-eq in fp32.
+  uint32_t qf[KSTEPS][NT][2];
+  float qinv[NT];     // 2^-eq of head nt*4 + c4
+  float qs[NG][NT];   // group sums of the scaled query of head nt*4 + c4
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int hq = nt * 4 + (g8 >> 1);
+    const bool live = hq < p.gq;
+    const float *qh = qbase + (long long)(live ? hq : 0) * D;
+    float x[KSTEPS][4];
+    float mx = 0.f;
+    float gs[NG];
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) gs[gi] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float v = live ? __ldg(qh + q_dim<FMT>(ks, c4, j)) * a.scale_log2 : 0.f;
+        x[ks][j] = v;
+        mx = fmaxf(mx, fabsf(v));
+        gs[(k_dim0<FMT>(ks) * NG) / D] += v;
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const int eq = min(norm_exp(mx, 14), 100);
+    const float fq = exp2i(max(eq, -126));
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) {
+      gs[gi] += __shfl_xor_sync(0xffffffffu, gs[gi], 1);
+      gs[gi] += __shfl_xor_sync(0xffffffffu, gs[gi], 2);
+    }
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float xs = x[ks][j] * fq;
+        const float hi = __half2float(__float2half_rn(xs));
+        v[j] = (g8 & 1) ? xs - hi : hi;
+      }
+      qf[ks][nt][0] = ptx::pack_f16x2(v[0], v[1]);
+      qf[ks][nt][1] = ptx::pack_f16x2(v[2], v[3]);
+    }
+    // Row group 2*c4 holds head nt*4 + c4.
+    qinv[nt] = __shfl_sync(0xffffffffu, exp2i(max(-eq, -126)), 8 * c4);
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) qs[gi][nt] = __shfl_sync(0xffffffffu, gs[gi], 8 * c4);
+  }
+
+  float o[MD][NT][4];
+#pragma unroll
+  for (int md = 0; md < MD; ++md)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[md][nt][e] = 0.f;
+  float m_run[NT], l_run[NT], z_run[NG][NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt] = -INFINITY;
+    l_run[nt] = 0.f;
+#pragma unroll
+    for (int gi = 0; gi < NG; ++gi) z_run[gi][nt] = 0.f;
+  }
+  // O accumulates sum_t (p_t * scale_t * 2^ev) * code_t; ev is re-chosen per
+  // stage (exactly, by powers of two) so the fp16 hi/lo parts keep full
+  // precision.
+  int ev_run = 14;
+
+  const uint32_t pscr = sbase + p.off_pscr + warp * p.pscr_warp;
+  const int st_row = lane & 7, st_mat = (lane >> 3) & 1;
+  // ldmatrix lane roles: token row within a 16-token m-tile, chunk within a
+  // pair. Offsets of this lane's rows inside a stage, per m-tile and per
+  // chunk pair, computed once (rows start at multiples of 8, so the swizzle
+  // term depends on the lane only).
+  uint32_t off_mt[MT], off_xi[NCH / 2];
+  {
+    const int ld_tok = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int ld_chp = lane >> 4;
+    const uint32_t xorv = BOXX == 128 ? (uint32_t)((ld_tok & 7) << 4)
+                          : BOXX == 64 ? (uint32_t)(((ld_tok & 7) >> 1) << 4)
+                                       : (uint32_t)(((ld_tok & 7) >> 2) << 4);
+    const uint32_t tbox_mask = (1u << tbs) - 1u;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint32_t t16 = (uint32_t)mt * 16u;
+      off_mt[mt] = (t16 >> tbs) * p.box_bytes + (uint32_t)((warp << tbs) + ld_tok) * BOXX +
+                   (t16 & tbox_mask) * BOXX;
+    }
+#pragma unroll
+    for (int xi = 0; xi < NCH / 2; ++xi) {
+      const int ch = 2 * xi + ld_chp;
+      off_xi[xi] = (uint32_t)((2 * xi) / CPB) * (uint32_t)p.npg * p.box_bytes +
+                   (((uint32_t)(ch % CPB) * 16u) ^ xorv);
+    }
+  }
+  // Metadata of (this warp's head, token t): words at meta + (warp*TB + t)*GPR*4.
+  const uint32_t meta_lane = (uint32_t)((warp * TB + g8) * GPR * 4);
+
+  int s = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int i = 0; i < ntiles; ++i) {
+    if (!warp_wait(bar_full + 8u * s, phase, &s_abort)) {
+      ok = false;
+      break;
+    }
+    const int tt = t0 + i * TB;
+    const int vt = min(TB, t1 - tt);  // valid tokens in this stage
+    const uint32_t sk = sbase + s * p.stage_bytes;
+    const uint32_t sv = sk + p.kv_bytes;
+    const uint32_t smk = sv + p.kv_bytes;
+    const uint32_t smv = smk + p.meta_bytes;
+
+    // One stage; FULL (every token valid) drops the masking.
+    auto stage = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
+      const int nmt = FULL ? MT : (vt + 15) >> 4;
+
+      // f16 rows past the sequence end may hold any bits (NaN); zero this
+      // warp's V rows there so 0 * NaN never reaches the accumulators.
+      if (!FULL && FMT == 0 && vt < nmt * 16) {
+        const uint32_t tbox_mask = (1u << tbs) - 1u;
+        for (int t = vt; t < nmt * 16; ++t) {
+          const uint32_t pg = (uint32_t)(t >> tbs), tl = (uint32_t)t & tbox_mask;
+          for (int ch = lane; ch < NCH; ch += 32) {
+            const uint32_t xb = (uint32_t)(ch / CPB);
+            const uint32_t lin = (((uint32_t)warp << tbs) + tl) * BOXX + (uint32_t)(ch % CPB) * 16u;
+            const uint32_t ad = sv + (xb * (uint32_t)p.npg + pg) * p.box_bytes + (lin ^ ((lin >> 3) & SWZ));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(ad), "r"(0) : "memory");
+          }
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+      }
+
+      // Metadata words of this thread's tokens (rows g8, g8 + 8 of m-tile mt).
+      auto load_meta = [&](uint32_t base, int mt, int rr, uint32_t (&w)[NG]) {
+        const uint32_t ad = base + meta_lane + (uint32_t)((mt * 16 + rr * 8) * GPR * 4);
+        if (GPR == 1) {
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[0]) : "r"(ad));
+        } else if (GPR == 2) {
+          asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[NG > 1 ? 1 : 0]) : "r"(ad));
+        } else if (GPR == 4) {
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(w[0]), "=r"(w[NG > 1 ? 1 : 0]), "=r"(w[NG > 2 ? 2 : 0]), "=r"(w[NG > 3 ? 3 : 0])
+                       : "r"(ad));
+        }
+      };
+
+      // ---- scores of every 16-token m-tile of the stage
+      float sc[MT][NT][2];
+      float tmax[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) tmax[nt] = -INFINITY;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = -INFINITY;
+        if (FULL || mt < nmt) {
+          float acc[NG][NT][4];
+#pragma unroll
+          for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[gi][nt][e] = 0.f;
+#pragma unroll
+          for (int xi = 0; xi < NCH / 2; ++xi) {
+            uint32_t r0, r1, r2, r3;
+            ptx::ldsm_x4(sk + off_mt[mt] + off_xi[xi], r0, r1, r2, r3);
+            if (FMT == 0) {
+              const uint32_t af[4] = {r0, r1, r2, r3};
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) ptx::mma_f16(acc[0][nt], af, qf[xi][nt][0], qf[xi][nt][1]);
+            } else if (FMT == 1) {
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const uint32_t ra = hf ? r2 : r0, rb = hf ? r3 : r1;
+                const uint32_t af[4] = {u8pair(ra, 0x4140u), u8pair(rb, 0x4140u), u8pair(ra, 0x4342u),
+                                        u8pair(rb, 0x4342u)};
+                const int ks = 2 * xi + hf;
+                const int gi = (k_dim0<FMT>(ks) * NG) / D;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) ptx::mma_f16(acc[gi][nt], af, qf[ks][nt][0], qf[ks][nt][1]);
+              }
+            } else {
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const uint32_t ra = hf ? r2 : r0, rb = hf ? r3 : r1;
+                const uint32_t ra8 = ra >> 8, rb8 = rb >> 8;
+                const uint32_t afa[4] = {u4lo(ra), u4lo(rb), u4hi(ra), u4hi(rb)};
+                const uint32_t afb[4] = {u4lo(ra8), u4lo(rb8), u4hi(ra8), u4hi(rb8)};
+                const int ksa = 4 * xi + 2 * hf;
+                const int gi = (k_dim0<FMT>(ksa) * NG) / D;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                  ptx::mma_f16(acc[gi][nt], afa, qf[ksa][nt][0], qf[ksa][nt][1]);
+                  ptx::mma_f16(acc[gi][nt], afb, qf[ksa + 1][nt][0], qf[ksa + 1][nt][1]);
+                }
+              }
+            }
+          }
+          // Combine parts and groups for rows g8 and g8 + 8 of the m-tile:
+          // s = 2^-eq * sum_g scale_g * dot_g + sum_g zero'_g * qsum_g.
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            float ksc[NG], kz[NG];
+            if (GPR > 0) {
+              uint32_t w[NG];
+              load_meta(smk, mt, rr, w);
+#pragma unroll
+              for (int gi = 0; gi < NG; ++gi) {
+                const float2 f = meta_sz(w[gi]);
+                ksc[gi] = f.x;
+                kz[gi] = fmaf(CENTRE, f.x, f.y);
+              }
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              float v;
+              if (GPR > 0) {
+                float dsum = 0.f, zq = 0.f;
+#pragma unroll
+                for (int gi = 0; gi < NG; ++gi) {
+                  dsum = fmaf(ksc[gi], acc[gi][nt][2 * rr] + acc[gi][nt][2 * rr + 1], dsum);
+                  zq = fmaf(kz[gi], qs[gi][nt], zq);
+                }
+                v = fmaf(dsum, qinv[nt], zq);
+              } else {
+                v = (acc[0][nt][2 * rr] + acc[0][nt][2 * rr + 1]) * qinv[nt];
+              }
+              if (!FULL && mt * 16 + g8 + rr * 8 >= vt) v = -INFINITY;
+              sc[mt][nt][rr] = v;
+              tmax[nt] = fmaxf(tmax[nt], v);
+            }
+          }
+        }
+      }
+
+      // ---- value pre-scale for this stage: 2^ev * max(V scale) in [2^13, 2^14)
+      int ev = 14;
+      if (GPR > 0) {
+        uint32_t vbits = 0;  // fp16 bits of positive scales order like the values
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr)
+            if (FULL || mt * 16 + g8 + rr * 8 < vt) {
+              uint32_t w[NG];
+              load_meta(smv, mt, rr, w);
+#pragma unroll
+              for (int gi = 0; gi < NG; ++gi) vbits = max(vbits, w[gi] & 0x7FFFu);
+            }
+        vbits = max(vbits, __shfl_xor_sync(0xffffffffu, vbits, 4));
+        vbits = max(vbits, __shfl_xor_sync(0xffffffffu, vbits, 8));
+        vbits = max(vbits, __shfl_xor_sync(0xffffffffu, vbits, 16));
+        ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vbits)), 14), 100), -100);
+      }
+      const float fv = exp2i(max(min(ev, 127), -126));
+      const float fratio = exp2i(max(min(ev - ev_run, 127), -126));
+      ev_run = ev;
+
+      // ---- online softmax, one rescale per stage (O is rescaled when the
+      // stage's value product is folded in below)
+      float ao[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float mx = tmax[nt];
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[nt], mx);
+        const float alpha = exp2f(m_run[nt] - m_new);  // 0 on the first stage
+        m_run[nt] = m_new;
+        l_run[nt] *= alpha;
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) z_run[gi][nt] *= alpha;
+        ao[nt] = alpha * fratio;
+      }
+
+      // ---- probabilities: P'^T fragments of every m-tile, per value group,
+      // through a stmatrix.trans/ldmatrix round trip (C layout of S^T -> B
+      // layout of P^T)
+      uint32_t pb[MT][NG][NT][2];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        if (FULL || mt < nmt) {
+          float pr[NT][2];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              const float pv = exp2f(sc[mt][nt][rr] - m_run[nt]);  // 0 for masked rows
+              pr[nt][rr] = pv;
+              l_run[nt] += pv;
+            }
+          // Value scale (times 2^ev) and centred zero of this thread's two
+          // tokens; 0 for masked rows so stale bits never leak in.
+          float vsc[NG][2], vz[NG][2];
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const bool valid = FULL || mt * 16 + g8 + rr * 8 < vt;
+            if (GPR > 0) {
+              uint32_t w[NG];
+              load_meta(smv, mt, rr, w);
+#pragma unroll
+              for (int gi = 0; gi < NG; ++gi) {
+                const float2 f = meta_sz(w[gi]);
+                vsc[gi][rr] = valid ? f.x * fv : 0.f;
+                vz[gi][rr] = valid ? fmaf(CENTRE, f.x, f.y) : 0.f;
+              }
+            } else {
+              vsc[0][rr] = valid ? fv : 0.f;
+              vz[0][rr] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint32_t w0 = split_hi_lo(pr[nt][0] * vsc[gi][0]);
+              const uint32_t w1 = split_hi_lo(pr[nt][1] * vsc[gi][1]);
+              if (GPR > 0) {
+                z_run[gi][nt] = fmaf(pr[nt][0], vz[gi][0], z_run[gi][nt]);
+                z_run[gi][nt] = fmaf(pr[nt][1], vz[gi][1], z_run[gi][nt]);
+              }
+              stsm_x2_t(pscr + (uint32_t)((gi * NT + nt) * 384 + st_row * 48 + st_mat * 16), w0, w1);
+            }
+          __syncwarp();
+#pragma unroll
+          for (int gi = 0; gi < NG; ++gi)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              ldsm_x2(pscr + (uint32_t)((gi * NT + nt) * 384 + st_row * 48 + st_mat * 16),
+                      pb[mt][gi][nt][0], pb[mt][gi][nt][1]);
+          __syncwarp();
+        }
+      }
+
+      // ---- value product. Each chunk pair's d-tiles accumulate this stage's
+      // tokens in fresh tensor-core accumulators (a handful of MMA additions),
+      // then fold into the running fp32 O with one round-to-nearest FFMA that
+      // also applies the stage's rescale: tensor-core accumulation truncates,
+      // so long runs of MMA additions into one register would bias the sum.
+      constexpr int DT = FMT == 0 ? 1 : FMT == 1 ? 2 : 4;  // d-tiles per chunk pair
+#pragma unroll
+      for (int xi = 0; xi < NCH / 2; ++xi) {
+        float tacc[DT][NT][4];
+#pragma unroll
+        for (int k = 0; k < DT; ++k)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tacc[k][nt][e] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          if (FULL || mt < nmt) {
+            uint32_t r0, r1, r2, r3;
+            ptx::ldsm_x4_t(sv + off_mt[mt] + off_xi[xi], r0, r1, r2, r3);
+            if (FMT == 0) {
+              const uint32_t af[4] = {r0, r2, r1, r3};
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) ptx::mma_f16(tacc[0][nt], af, pb[mt][0][nt][0], pb[mt][0][nt][1]);
+            } else if (FMT == 1) {
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const uint32_t ra = hf ? r2 : r0, rb = hf ? r3 : r1;
+                const uint32_t af[4] = {u8pair(ra, 0x4240u), u8pair(ra, 0x4341u), u8pair(rb, 0x4240u),
+                                        u8pair(rb, 0x4341u)};
+                const int gi = (v_dim0<FMT>(2 * xi + hf) * NG) / D;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  ptx::mma_f16(tacc[hf][nt], af, pb[mt][gi][nt][0], pb[mt][gi][nt][1]);
+              }
+            } else {
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const uint32_t ra = hf ? r2 : r0, rb = hf ? r3 : r1;
+                const uint32_t ra8 = ra >> 8, rb8 = rb >> 8;
+                const int ch = 2 * xi + hf;
+                const int gi = (v_dim0<FMT>(2 * ch) * NG) / D;
+                const uint32_t af0[4] = {u4lo(ra), u4hi(ra), u4lo(rb), u4hi(rb)};
+                const uint32_t af1[4] = {u4lo(ra8), u4hi(ra8), u4lo(rb8), u4hi(rb8)};
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                  ptx::mma_f16(tacc[2 * hf][nt], af0, pb[mt][gi][nt][0], pb[mt][gi][nt][1]);
+                  ptx::mma_f16(tacc[2 * hf + 1][nt], af1, pb[mt][gi][nt][0], pb[mt][gi][nt][1]);
+                }
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < DT; ++k)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              o[DT * xi + k][nt][e] = fmaf(o[DT * xi + k][nt][e], ao[nt], tacc[k][nt][e]);
+      }
+    };
+    if (vt == TB)
+      stage(std::true_type{});
+    else
+      stage(std::false_type{});
+
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(bar_empty + 8u * s);
+    if (++s == p.stages) {
+      s = 0;
+      phase ^= 1u;
+    }
+  }
+
+  // ---------------------------------------------------------------- epilogue
+  if (!ok) {
+    if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+    s_abort = 1;
+    return;
+  }
+  // Reduce the per-thread sums over the 8 row groups.
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l_run[nt] += __shfl_xor_sync(0xffffffffu, l_run[nt], off);
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) z_run[gi][nt] += __shfl_xor_sync(0xffffffffu, z_run[gi][nt], off);
+    }
+  }
+  const float finv = exp2i(max(min(-ev_run, 127), -126));
+  // O = (O_hi + O_lo) * 2^-ev + zero term; one query head per (n-tile, c4).
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int hq = nt * 4 + c4;
+    if (hq < p.gq) {
+      const long long head = (long long)b * a.H + (long long)h * p.gq + hq;
+      const float L = l_run[nt];
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      float *dst;
+      if (p.final_out) {
+        dst = a.out + head * D;
+      } else {
+        dst = a.part_o + (head * p.splits + split) * D;
+        if (g8 == 0) {
+          a.part_ml[(head * p.splits + split) * 2] = m_run[nt];
+          a.part_ml[(head * p.splits + split) * 2 + 1] = L;
+        }
+      }
+#pragma unroll
+      for (int md = 0; md < MD; ++md) {
+        const int gi = (v_dim0<FMT>(md) * NG) / D;
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int d = v_dim<FMT>(md, g8 + rr * 8);
+          float val = (o[md][nt][2 * rr] + o[md][nt][2 * rr + 1]) * finv;
+          if (GPR > 0) val += z_run[gi][nt];
+          dst[d] = p.final_out ? val * inv : val;
+        }
+      }
+    }
+  }
+}
+
+// Log-sum-exp merge of the split partials (runtime/kvf_kernels.cuh:288-306):
+//   M = max_s m_s,  L = sum_s l_s 2^(m_s - M),  out = sum_s o_s 2^(m_s - M) / L
+// (splits with m_s = -inf contribute nothing; L = 0 gives 0). One block per
+// (query head, sequence, 32 output columns); warp w takes splits w, w+8, ...,
+// issuing all of its loads before using any (one L2 round trip for up to
+// 256 splits), and the warps' partial (M, L, O) are combined the same way.
+constexpr int kMergeWarps = 8;
+constexpr int kMergeUnroll = 32;
+
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args a, int d) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float s_m[kMergeWarps], s_l[kMergeWarps];
+  __shared__ float s_o[kMergeWarps][32];
+  const long long head = (long long)blockIdx.y * a.H + blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.z * 32 + lane;
+  const bool colok = col < d;
+  const int S = a.splits;
+  const float *ml = a.part_ml + head * S * 2;
+  const float *po = a.part_o + head * (long long)S * d;
+
+  float M = -INFINITY, L = 0.f, O = 0.f;
+  for (int base = warp; base < S; base += kMergeWarps * kMergeUnroll) {
+    float ms[kMergeUnroll], ls[kMergeUnroll], os[kMergeUnroll];
+#pragma unroll
+    for (int k = 0; k < kMergeUnroll; ++k) {
+      const int sp = base + k * kMergeWarps;
+      const bool v = sp < S;
+      ms[k] = v ? __ldcg(ml + 2 * sp) : -INFINITY;
+      ls[k] = v ? __ldcg(ml + 2 * sp + 1) : 0.f;
+      os[k] = (v && colok) ? __ldcg(po + (long long)sp * d + col) : 0.f;
+    }
+    float mx = M;
+#pragma unroll
+    for (int k = 0; k < kMergeUnroll; ++k) mx = fmaxf(mx, ms[k]);
+    if (mx == -INFINITY) continue;
+    const float r = exp2f(M - mx);  // 0 when M is -inf
+    L *= r;
+    O *= r;
+#pragma unroll
+    for (int k = 0; k < kMergeUnroll; ++k) {
+      const float w = ms[k] == -INFINITY ? 0.f : exp2f(ms[k] - mx);
+      L = fmaf(ls[k], w, L);
+      O = fmaf(os[k], w, O);
+    }
+    M = mx;
+  }
+  if (lane == 0) {
+    s_m[warp] = M;
+    s_l[warp] = L;
+  }
+  s_o[warp][lane] = O;
+  __syncthreads();
+  if (warp == 0) {
+    float Mt = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, s_m[w]);
+    float Lt = 0.f, Ot = 0.f;
+    if (Mt != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kMergeWarps; ++w) {
+        const float wt = s_m[w] == -INFINITY ? 0.f : exp2f(s_m[w] - Mt);
+        Lt = fmaf(s_l[w], wt, Lt);
+        Ot = fmaf(s_o[w][lane], wt, Ot);
+      }
+    }
+    if (colok) a.out[head * d + col] = Lt > 0.f ? Ot / Lt : 0.f;
+  }
+}
+
+} // namespace kvfb

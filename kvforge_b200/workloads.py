@@ -1,0 +1,97 @@
+"""The benchmark workloads and their seeded synthetic inputs.
+
+Shapes are the five configurations the reference's headline metric is quoted
+on (decode-attention us/step and effective KV TB/s). Inputs are synthetic:
+seeded N(0,1) queries and keys/values generated on the device, with the
+per-configuration variations (fp16-representable queries, outlier channels,
+ragged sequence lengths, random page tables). There is no dataset.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+import torch
+
+from ._native import FMT_F16, FMT_INT4, FMT_INT8, ORD_HEAD, ORD_TOKEN
+from .layout import Placement
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    B: int
+    H: int
+    Hkv: int
+    d: int
+    n: int                      # tokens per sequence (the longest, when ragged)
+    fmt: int
+    group: int
+    place: Placement
+    ragged: Optional[tuple] = None   # (lo, hi): n_b ~ U[lo, hi], seeded
+    outlier_frac: float = 0.0        # fraction of (KV head, channel) pairs scaled x8
+    q_fp16: bool = False             # queries rounded to fp16 values
+    shard: str = "replicas"          # "replicas", "splitkv" or "kvheads" across GPUs
+    seed: int = 1
+
+    @property
+    def fmt_name(self) -> str:
+        return {FMT_F16: "f16", FMT_INT8: f"int8:{self.group}", FMT_INT4: f"int4:{self.group}"}[self.fmt]
+
+    def seq_lens(self) -> Optional[np.ndarray]:
+        if self.ragged is None:
+            return None
+        lo, hi = self.ragged
+        rng = np.random.default_rng(self.seed + 1000)
+        return rng.integers(lo, hi + 1, size=self.B).astype(np.int32)
+
+    def config(self) -> dict:
+        return {
+            "workload": self.name, "B": self.B, "H": self.H, "Hkv": self.Hkv, "d": self.d,
+            "n": self.n if self.ragged is None else f"U[{self.ragged[0]},{self.ragged[1]}]",
+            "kv_format": self.fmt_name, "layout": self.place.name,
+        }
+
+
+CONFIGS = {
+    w.name: w
+    for w in [
+        Workload("mha_b1_h32_n4096_f16_hm", 1, 32, 32, 128, 4096, FMT_F16, 0,
+                 Placement(ORD_HEAD, False, 0), q_fp16=True),
+        Workload("llama3_8b_gqa_b1_n32768_int8g64_tm", 1, 32, 8, 128, 32768, FMT_INT8, 64,
+                 Placement(ORD_TOKEN, False, 0), outlier_frac=0.01),
+        Workload("paged_gqa_b8_n2k_8k_f16_tm_p16", 8, 32, 8, 128, 8192, FMT_F16, 0,
+                 Placement(ORD_TOKEN, True, 16), ragged=(2048, 8192)),
+        Workload("long_gqa_b1_n65536_int4g32_hm", 1, 32, 8, 128, 65536, FMT_INT4, 32,
+                 Placement(ORD_HEAD, False, 0), shard="splitkv"),
+        Workload("llama3_70b_b64_n16384_int8g64_tm_p16", 64, 64, 8, 128, 16384, FMT_INT8, 64,
+                 Placement(ORD_TOKEN, True, 16), shard="kvheads"),
+    ]
+}
+CONFIG_ORDER = list(CONFIGS)
+# The configuration the headline metric is quoted on at one GPU.
+HEADLINE = CONFIG_ORDER[1]
+
+
+def generate(w: Workload, device, seed: Optional[int] = None):
+    """Seeded inputs for workload w: q [B,H,D], K and V [B,Hkv,n,D] (float32,
+    logical order, on `device`) and seq_lens (np.int32 [B] or None)."""
+    seed = w.seed if seed is None else seed
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    q = torch.randn((w.B, w.H, w.d), generator=g, device=device, dtype=torch.float32)
+    if w.q_fp16:
+        q = q.half().float()
+    K = torch.randn((w.B, w.Hkv, w.n, w.d), generator=g, device=device, dtype=torch.float32)
+    V = torch.randn((w.B, w.Hkv, w.n, w.d), generator=g, device=device, dtype=torch.float32)
+    if w.outlier_frac > 0:
+        count = max(1, int(round(w.outlier_frac * w.Hkv * w.d)))
+        for X in (K, V):
+            idx = torch.randperm(w.Hkv * w.d, generator=g, device=device)[:count]
+            hs, cs = idx // w.d, idx % w.d
+            X[:, hs, :, cs] *= 8.0
+    return q, K, V, w.seq_lens()
+
+
+__all__ = ["Workload", "CONFIGS", "CONFIG_ORDER", "HEADLINE", "generate"]
