@@ -132,6 +132,35 @@ unsigned kvf_b200_device_errors(void);
 cudaError_t kvf_b200_quantize(int fmt, int d, int group, const float *x, long long rows,
                               unsigned char *data, void *meta, cudaStream_t stream);
 
+/* Bytes of device scratch behind kvf_b200_decode_noalloc (8 MiB). */
+#define KVF_B200_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* kvf_b200_decode for callers that cannot allocate device memory. It has no
+ * counterpart in the reference, whose harnesses always allocate the split
+ * workspace themselves (alloc_buffers).
+ *
+ * Callers such as a serving engine that reserved all device memory for its
+ * KV pool at start-up, or a plugin whose framework owns every allocation,
+ * cannot cudaMalloc the part_o / part_ml workspace that splits > 1 needs.
+ * This entry point ignores a->part_o and a->part_ml and keeps the partials in
+ * a static device array of KVF_B200_NOALLOC_SCRATCH_BYTES inside the library
+ * (held by every GPU that loads the library until the process exits); it
+ * calls no allocator. The caller still passes q, the cache, out and the
+ * other inputs. Limits and rules:
+ *   - B * H * splits * (d + 2) * 4 bytes (plus alignment) must fit the
+ *     scratch; larger requests return cudaErrorInvalidValue (use fewer
+ *     splits, or kvf_b200_decode with your own workspace);
+ *   - all calls on a device share the one array: calls that overlap on the
+ *     GPU (concurrent streams) race and corrupt each other's partials.
+ *     Nothing needs clearing between calls: every call writes each partial
+ *     it later reads;
+ *   - the first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ * splits <= 1 needs no scratch and behaves exactly like kvf_b200_decode. */
+cudaError_t kvf_b200_decode_noalloc(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                                    cudaStream_t stream);
+
 /* Library version string. */
 const char *kvf_b200_version(void);
 

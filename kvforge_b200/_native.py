@@ -70,6 +70,7 @@ _lib = None
 SIGNATURES = [
     ("kvf_b200_decode", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_merge", c_int, [ctypes.POINTER(KvfArgs), c_int, c_void_p]),
+    ("kvf_b200_decode_noalloc", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_launch_variant", c_int, [c_char_p, ctypes.POINTER(KvfArgs), c_void_p]),
     ("kvf_b200_variant_count", c_int, []),
     ("kvf_b200_variant_name", c_char_p, [c_int]),

@@ -417,3 +417,67 @@ extern "C" unsigned kvf_b200_device_errors(void) {
 }
 
 extern "C" const char *kvf_b200_version(void) { return "kvforge_b200 0.1 (sm_100a)"; }
+
+// ---------------------------------------------------------------------------
+// Decode without any allocation by the caller or by this library.
+//
+// Some callers cannot call cudaMalloc: a serving engine that reserved all of
+// device memory for its KV page pool at start-up (any later allocation can
+// fail, and cudaMalloc may synchronise the device in the middle of a decode
+// step), or a plugin whose host framework owns and accounts for every device
+// allocation and hands it nothing but the tensors of the call. For them the
+// split partials live in this file-scope device array, which every GPU that
+// loads the library holds until the process exits.
+namespace kvfb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = KVF_B200_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch array, looked up once per device with that
+// device current. In host code the array's name is only a host-side stand-in,
+// never a device address, so it is never passed to a kernel directly.
+void *noalloc_scratch_address(cudaError_t &err) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void *addr[kMaxDevices] = {};
+  int dev = 0;
+  err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= kMaxDevices) {
+    err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess) return nullptr;
+    addr[dev] = p;
+  }
+  err = cudaSuccess;
+  return addr[dev];
+}
+
+} // namespace
+} // namespace kvfb
+
+extern "C" cudaError_t kvf_b200_decode_noalloc(const kvf_args *a, int fmt, int d, int g, int ord,
+                                               int paged, cudaStream_t stream) {
+  if (!a) return cudaErrorInvalidValue;
+  if (a->splits <= 1 || a->B == 0) return kvf_b200_decode(a, fmt, d, g, ord, paged, stream);
+  if (a->B < 0 || a->H <= 0 || (d != 64 && d != 128)) return cudaErrorInvalidValue;
+  // part_ml [B][H][splits][2] then part_o [B][H][splits][D], both fp32.
+  const size_t heads = (size_t)a->B * (size_t)a->H * (size_t)a->splits;
+  const size_t ml_bytes = (heads * 2 * sizeof(float) + 255) & ~(size_t)255;
+  const size_t o_bytes = heads * (size_t)d * sizeof(float);
+  if (heads > kvfb::kNoAllocScratchBytes || ml_bytes + o_bytes > kvfb::kNoAllocScratchBytes)
+    return cudaErrorInvalidValue;  // partials exceed KVF_B200_NOALLOC_SCRATCH_BYTES
+  cudaError_t err;
+  unsigned char *base = static_cast<unsigned char *>(kvfb::noalloc_scratch_address(err));
+  if (!base) return err;
+  kvf_args b = *a;
+  b.part_ml = reinterpret_cast<float *>(base);
+  b.part_o = reinterpret_cast<float *>(base + ml_bytes);
+  return kvf_b200_decode(&b, fmt, d, g, ord, paged, stream);
+}
