@@ -45,11 +45,13 @@ struct Args {
   int max_blocks;              // pages per sequence in the block table
   float scale_log2;            // softmax scale * log2(e)
   const int *seq_lens;         // [B] tokens per sequence; nullptr = n for all
+  unsigned *split_sem;         // [B][Hkv] zeroed counters for the in-kernel merge; nullptr = two launches
 };
 
 static_assert(sizeof(Args) == sizeof(kvf_args), "kvf::Args must mirror kvf_args");
 static_assert(offsetof(Args, scale_log2) == offsetof(kvf_args, scale_log2), "layout");
 static_assert(offsetof(Args, seq_lens) == offsetof(kvf_args, seq_lens), "layout");
+static_assert(offsetof(Args, split_sem) == offsetof(kvf_args, split_sem), "layout");
 
 inline const kvf_args *c_args(const Args &a) { return reinterpret_cast<const kvf_args *>(&a); }
 

@@ -52,6 +52,13 @@ enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
  *   block_shift  log2(tokens per page), paged layouts
  *   scale_log2   softmax scale * log2(e)
  *   seq_lens     [B] tokens of each sequence (each <= n); NULL = all n.
+ *   split_sem    [B][Hkv] unsigned counters, zero before the first call and
+ *                left zero by every call. When given (and splits > 1) the
+ *                last block to finish each (sequence, KV head) merges that
+ *                head's split partials itself, so no separate merge kernel
+ *                runs; part_o/part_ml are still written and read. NULL = the
+ *                reference's two-launch scheme. Calls sharing one array must
+ *                not overlap on the GPU.
  */
 typedef struct kvf_args {
   const float *q;
@@ -72,6 +79,7 @@ typedef struct kvf_args {
   float scale_log2;
   /* ---- additions (zero = reference behaviour) ---- */
   const int *seq_lens;
+  unsigned *split_sem;
 } kvf_args;
 
 /* One decode step: the sm_100a counterpart of

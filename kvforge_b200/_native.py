@@ -20,7 +20,7 @@ FMT_NAMES = {"f16": FMT_F16, "int8": FMT_INT8, "int4": FMT_INT4}
 
 class KvfArgs(ctypes.Structure):
     """Mirror of kvf_args / kvf::Args (runtime/kvf_kernels.cuh:29-46) plus the
-    appended seq_lens field."""
+    appended seq_lens and split_sem fields."""
 
     _fields_ = [
         ("q", c_void_p),
@@ -43,6 +43,7 @@ class KvfArgs(ctypes.Structure):
         ("max_blocks", c_int),
         ("scale_log2", c_float),
         ("seq_lens", c_void_p),
+        ("split_sem", c_void_p),
     ]
 
 

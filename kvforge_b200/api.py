@@ -134,20 +134,29 @@ class KVCache:
 
 @dataclass
 class Workspace:
-    """Split partials: part_o [B][H][splits][D] and part_ml [B][H][splits][2]."""
+    """Split partials: part_o [B][H][splits][D] and part_ml [B][H][splits][2].
+
+    ``split_sem`` (zeroed uint32 counters, one per (sequence, query head),
+    enough for any Hkv <= H) lets the kernel merge the splits itself: the last
+    block to finish a (sequence, KV head) merges its partials and resets the
+    counter. ``fused=False`` leaves it out, and a separate merge kernel runs as
+    in the reference.
+    """
 
     splits: int
     part_o: Optional[torch.Tensor]
     part_ml: Optional[torch.Tensor]
+    split_sem: Optional[torch.Tensor] = None
 
     @classmethod
-    def allocate(cls, B: int, H: int, d: int, splits: int, device) -> "Workspace":
+    def allocate(cls, B: int, H: int, d: int, splits: int, device, fused: bool = True) -> "Workspace":
         if splits <= 1:
             return cls(1, None, None)
         return cls(
             splits,
             torch.empty((B, H, splits, d), dtype=torch.float32, device=device),
             torch.empty((B, H, splits, 2), dtype=torch.float32, device=device),
+            torch.zeros((B * H,), dtype=torch.int32, device=device) if fused else None,
         )
 
 
@@ -169,6 +178,7 @@ def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace)
     a.out = out.data_ptr()
     a.part_o = ws.part_o.data_ptr() if ws.part_o is not None else None
     a.part_ml = ws.part_ml.data_ptr() if ws.part_ml is not None else None
+    a.split_sem = ws.split_sem.data_ptr() if ws.split_sem is not None else None
     a.B, a.H, a.Hkv, a.n = B, H, cache.Hkv, cache.n
     a.splits = ws.splits
     a.warps = 4

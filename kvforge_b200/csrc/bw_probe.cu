@@ -10,6 +10,8 @@
 //   kvf_bw_probe [--device 0] [--mb 2048] [--name b200]
 #include "ptx.cuh"
 
+#include <cuda.h>
+
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
@@ -88,6 +90,50 @@ __global__ void __launch_bounds__(32) bulk_stream(const uint8_t *p, size_t bytes
                     chunk, bar, pol);
       ++issued;
     }
+  }
+}
+
+// One thread per CTA streams a token range of one head group through a ring
+// of `stages` stages; each stage is `nxb` tiled TMA copies of [128 B,
+// box_rows tokens, 4 heads] (the decode kernels' box shape) from a 4-D view
+// (x, token, head, 1) of a cache with 8 KV heads. CTA pairs take head groups
+// 0-3 and 4-7 of the same tokens.
+__global__ void __launch_bounds__(32) tma_tile_stream(const __grid_constant__ CUtensorMap tm, int nxb,
+                                                      int box_rows, int stages, int rows_per_block) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[16];
+  if (threadIdx.x != 0) return;
+  uint8_t *buf = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
+  for (int s = 0; s < stages; ++s) ptx::mbar_init(ptx::smem_u32(&bars[s]), 1);
+  ptx::fence_barrier_init();
+  const uint64_t pol = ptx::policy_evict_first();
+  const uint32_t box_bytes = 128u * (uint32_t)box_rows * 4u;
+  const int n = rows_per_block / box_rows;
+  const int h0 = (blockIdx.x & 1) * 4;
+  const int row0 = (blockIdx.x >> 1) * rows_per_block;
+  uint32_t phase = 0;
+  int issued = 0;
+  auto issue = [&](int k, int s) {
+    const uint32_t bar = ptx::smem_u32(&bars[s]);
+    ptx::mbar_arrive_expect_tx(bar, box_bytes * (uint32_t)nxb);
+    for (int xb = 0; xb < nxb; ++xb)
+      ptx::tma_g2s_4d(ptx::smem_u32(buf + ((size_t)s * nxb + xb) * box_bytes), &tm, xb * 128,
+                      row0 + k * box_rows, h0, 0, bar, pol);
+  };
+  for (; issued < stages && issued < n; ++issued) issue(issued, issued);
+  for (int done = 0; done < n; ++done) {
+    const int s = done % stages;
+    if (!ptx::mbar_wait(ptx::smem_u32(&bars[s]), (phase >> s) & 1u)) {
+      atomicExch(&g_probe_err, 1u);
+      for (int k = done; k < issued; ++k) {
+        const int s2 = k % stages;
+        ptx::mbar_wait(ptx::smem_u32(&bars[s2]), (phase >> s2) & 1u);
+        phase ^= 1u << s2;
+      }
+      return;
+    }
+    phase ^= 1u << s;
+    if (issued < n) issue(issued++, s);
   }
 }
 
@@ -227,6 +273,58 @@ int main(int argc, char **argv) {
                     per_sm, gbs);
         if (gbs > bw_bulk) { bw_bulk = gbs; best_chunk = chunk; best_stages = stages; best_ctas = per_sm; }
       }
+  // Tiled TMA stream with the decode kernels' box shapes: a [n_tok][8 heads]
+  // x row_bytes token-major tensor (rows of one head strided by 8 rows), box
+  // [128 B, box_rows tokens, 4 heads] (token-major) or a head-major tensor
+  // [8 heads][n_tok] x row_bytes with box [128 B, box_rows, 4 heads].
+  typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  void *encp = nullptr;
+  cudaDriverEntryPointQueryResult qres;
+  PROBE_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &encp, cudaEnableDefault, &qres));
+  EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(encp);
+  double bw_tile = 0;
+  for (int tm_layout : {1, 0})
+    for (int rb : {128, 256})
+      for (int box_rows : {16, 32, 64})
+        for (int stages : {2, 4, 6})
+          for (int per_sm : {1, 2}) {
+            const int heads = 8;
+            const size_t tokens = bytes / ((size_t)heads * rb);
+            cuuint64_t dims[4] = {(cuuint64_t)rb, (cuuint64_t)tokens, (cuuint64_t)heads, 1};
+            cuuint64_t strides[3];
+            strides[0] = tm_layout ? (cuuint64_t)heads * rb : (cuuint64_t)rb;
+            strides[1] = tm_layout ? (cuuint64_t)rb : (cuuint64_t)tokens * rb;
+            strides[2] = (cuuint64_t)tokens * heads * rb;
+            const cuuint32_t box[4] = {128u, (cuuint32_t)box_rows, 4u, 1u};
+            const cuuint32_t es[4] = {1, 1, 1, 1};
+            CUtensorMap tmap;
+            if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, buf, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+              std::printf("# tma_tile_stream encode failed (tm=%d rb=%d)\n", tm_layout, rb);
+              continue;
+            }
+            const int nxb = rb / 128;
+            const int stage_bytes = 128 * box_rows * 4 * nxb;
+            const int smem = stage_bytes * stages + 1024;
+            if (smem * per_sm > 220 * 1024 || smem > 227 * 1024) continue;
+            PROBE_CHECK(cudaFuncSetAttribute(tma_tile_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            const int ctas = (sms * per_sm) & ~1;
+            const int rows_per_block = (int)(tokens / (ctas / 2)) / box_rows * box_rows;
+            const float ms = tm.best_ms(
+                [&] { tma_tile_stream<<<ctas, 32, smem>>>(tmap, nxb, box_rows, stages, rows_per_block); }, 3);
+            const double moved = (double)ctas * rows_per_block * 4 * rb;
+            const double gbs = moved / (ms * 1e6);
+            std::printf("# tma_tile_stream %s row=%dB box=[128B x %d tok x 4 heads] x%d stage=%dKB stages=%d "
+                        "ctas/sm=%d: %.1f GB/s\n",
+                        tm_layout ? "token-major" : "head-major", rb, box_rows, nxb, stage_bytes / 1024, stages,
+                        per_sm, gbs);
+            bw_tile = std::max(bw_tile, gbs);
+          }
+
   unsigned perr = 0;
   PROBE_CHECK(cudaMemcpyFromSymbol(&perr, g_probe_err, 4));
   if (perr) std::printf("# WARNING: bulk_stream barrier wait timed out\n");

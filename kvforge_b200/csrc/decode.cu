@@ -8,11 +8,13 @@
 #include "kvforge_b200.h"
 
 #include "decode_kernel.cuh"
+#include "decode_tc.cuh"
 
 #include <cuda.h>
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -232,11 +234,19 @@ cudaError_t plan_launch(const kvf_args *a, const Shape &sh, Launch &L) {
   return cudaSuccess;
 }
 
+cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int boxx, int tbox, int heads,
+                            CUtensorMap &tk, CUtensorMap &tv);
+
 cudaError_t encode_maps(const kvf_args *a, const Shape &sh, const Plan &p, CUtensorMap &tk,
                         CUtensorMap &tv) {
+  return encode_maps_box(a, sh, p.rb, p.boxx, p.tbox, p.hh, tk, tv);
+}
+
+cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int boxx, int tbox, int heads,
+                            CUtensorMap &tk, CUtensorMap &tv) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  const cuuint64_t rb = (cuuint64_t)p.rb;
+  const cuuint64_t rb = (cuuint64_t)rbytes;
   cuuint64_t dims[4], strides[3];
   dims[0] = rb;
   dims[2] = (cuuint64_t)a->Hkv;
@@ -256,11 +266,11 @@ cudaError_t encode_maps(const kvf_args *a, const Shape &sh, const Plan &p, CUten
     strides[1] = sh.ord ? rb : n * rb;
     strides[2] = n * a->Hkv * rb;
   }
-  const cuuint32_t box[4] = {(cuuint32_t)p.boxx, (cuuint32_t)p.tbox, (cuuint32_t)p.hh, 1u};
+  const cuuint32_t box[4] = {(cuuint32_t)boxx, (cuuint32_t)tbox, (cuuint32_t)heads, 1u};
   const cuuint32_t es[4] = {1u, 1u, 1u, 1u};
-  const CUtensorMapSwizzle swz = p.boxx == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
-                                 : p.boxx == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUtensorMapSwizzle swz = boxx == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : boxx == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B;
   CUresult r = enc(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<unsigned char *>(a->k), dims,
                    strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -288,6 +298,128 @@ cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, merge_kernel, args, d);
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core (tcgen05) path: int8 rows of 128 dimensions.
+
+template <int GPR, int NH> struct TK {
+  static void *fn() { return reinterpret_cast<void *>(&decode_tc_kernel<GPR, NH>); }
+};
+
+void *tc_kernel_for(int gpr, int nh) {
+#define KVFB_TC(G, N) \
+  if (gpr == G && nh == N) return TK<G, N>::fn();
+  KVFB_TC(1, 4) KVFB_TC(1, 8) KVFB_TC(2, 4) KVFB_TC(2, 8)
+#undef KVFB_TC
+  return nullptr;
+}
+
+// KVF_B200_TC=0 in the environment selects the mma.sync kernels for every
+// format (for A/B measurements); the default uses tcgen05 where it applies.
+bool tc_enabled() {
+  const char *e = std::getenv("KVF_B200_TC");
+  return !(e && e[0] == '0');
+}
+
+uint32_t tc_misc_bytes(int gpr, int nh) {
+  size_t n = 0;
+  if (gpr == 1) n = nh == 4 ? sizeof(TcMisc<1, 4>) : sizeof(TcMisc<1, 8>);
+  else n = nh == 4 ? sizeof(TcMisc<2, 4>) : sizeof(TcMisc<2, 8>);
+  return (uint32_t)((n + 127) & ~(size_t)127);
+}
+
+// The tensor-core kernel takes one KV head per block; it wins once there are
+// enough (sequence, KV head) units to fill the GPU without many splits.
+// KVF_B200_TC=1 forces it for every shape it supports, KVF_B200_TC=0 never.
+constexpr int kTcMinUnits = 64;
+
+bool tc_applies(const Shape &sh, int units) {
+  const char *e = std::getenv("KVF_B200_TC");
+  const bool forced = e && e[0] == '1';
+  if (!tc_enabled() || sh.fmt != 1 || sh.d != 128 || (sh.gpr != 1 && sh.gpr != 2)) return false;
+  return forced || units >= kTcMinUnits;
+}
+
+struct TcLaunch {
+  TcPlan p;
+  void *fn = nullptr;
+  int blocks = 0;
+  int occupancy = 0;
+  int nh = 4;
+};
+
+cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
+  TcPlan &p = L.p;
+  std::memset(&p, 0, sizeof(p));
+  p.gq = a->H / a->Hkv;
+  L.nh = p.gq <= 4 ? 4 : 8;
+  L.fn = tc_kernel_for(sh.gpr, L.nh);
+  if (!L.fn) return cudaErrorInvalidValue;
+  const int ns = L.nh == 4 ? 16 : 32;
+  const int np = sh.gpr * ns;
+  p.paged = sh.paged;
+  p.tm = sh.ord;
+  p.bt_shift = sh.paged ? ilog2(sh.bt) : 0;
+  p.tbox = sh.paged ? std::min(kTcTokens, sh.bt) : kTcTokens;
+  p.tbox_shift = ilog2(p.tbox);
+  p.npg = kTcTokens / p.tbox;
+  p.meta_bytes = (uint32_t)((kTcTokens * sh.gpr * 4 + 127) & ~127);
+  p.stage_bytes = (2u * kTcTokens * 128u + 2u * p.meta_bytes + 1023u) & ~1023u;
+  p.ptile_bytes = (uint32_t)(np * kTcTokens);
+  const uint32_t qtile = (uint32_t)(ns * 128);
+  const uint32_t misc = tc_misc_bytes(sh.gpr, L.nh);
+  // 1024 bytes of slack for aligning the dynamic shared-memory base.
+  const uint32_t fixed = 1024u + ((qtile + 1023u) & ~1023u) + p.ptile_bytes + misc;
+  int occ = 2, stages = 0;
+  for (; occ >= 1; --occ) {
+    const int budget = std::min(kSmemPerBlockMax, kSmemPerSM / occ - kReservedPerBlock) - (int)fixed;
+    stages = std::min(8, budget / (int)p.stage_bytes);
+    if (stages >= 2) break;
+  }
+  if (stages < 2) return cudaErrorInvalidValue;
+  L.occupancy = occ;
+  p.stages = stages;
+  p.off_q = (uint32_t)stages * p.stage_bytes;
+  p.off_p = p.off_q + ((qtile + 1023u) & ~1023u);
+  p.off_misc = p.off_p + p.ptile_bytes;
+  p.smem_total = 1024u + p.off_misc + misc;
+  uint32_t cols = (uint32_t)(2 * sh.gpr * ns + np);
+  uint32_t alloc = 32;
+  while (alloc < cols) alloc <<= 1;
+  p.tmem_cols = alloc;
+  p.splits = a->splits;
+  p.final_out = a->splits == 1;
+  const int per = (a->n + a->splits - 1) / std::max(1, a->splits);
+  p.chunk = std::max(kTcTokens, (per + kTcTokens - 1) / kTcTokens * kTcTokens);
+  if (sh.paged && sh.bt > kTcTokens) p.chunk = (p.chunk + sh.bt - 1) / sh.bt * sh.bt;
+  L.blocks = a->B * a->Hkv * a->splits;
+  // The last block of a head merges in-kernel when counters are given and its
+  // scratch (a weight per split and query-head slot) fits in the idle ring.
+  p.merge_in_kernel = (a->split_sem && a->splits > 1 &&
+                       (size_t)(8 * a->splits + 8) * sizeof(float) <= (size_t)stages * p.stage_bytes)
+                          ? 1
+                          : 0;
+  return cudaSuccess;
+}
+
+cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream) {
+  TcLaunch L;
+  cudaError_t e = plan_tc(a, sh, L);
+  if (e != cudaSuccess) return e;
+  CUtensorMap tk, tv;
+  e = encode_maps_box(a, sh, 128, 128, L.p.tbox, 1, tk, tv);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
+  if (e != cudaSuccess) return e;
+  const kvf_args args = *a;
+  const TcPlan plan = L.p;
+  void *params[4] = {const_cast<kvf_args *>(&args), const_cast<TcPlan *>(&plan), &tk, &tv};
+  e = cudaLaunchKernel(L.fn, dim3((unsigned)L.blocks), dim3((unsigned)kTcThreads), params, L.p.smem_total, stream);
+  if (e != cudaSuccess) return e;
+  if (!L.p.final_out && !L.p.merge_in_kernel) e = launch_merge(a, sh.d, stream, true);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 } // namespace
 } // namespace kvfb
 
@@ -299,6 +431,7 @@ extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g,
   cudaError_t e = check_args(a, fmt, d, g, ord, paged, sh);
   if (e != cudaSuccess) return e;
   if (a->B == 0) return cudaSuccess;
+  if (tc_applies(sh, a->B * a->Hkv)) return launch_tc(a, sh, stream);
   Launch L;
   e = plan_launch(a, sh, L);
   if (e != cudaSuccess) return e;
@@ -330,13 +463,28 @@ extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int 
   Shape sh;
   cudaError_t e = check_args(a, fmt, d, 1, ord, paged, sh);
   if (e != cudaSuccess) return e;
+  if (tc_applies(sh, a->B * a->Hkv)) {
+    TcLaunch T;
+    e = plan_tc(a, sh, T);
+    if (e != cudaSuccess) return e;
+    if (buf && buf_len > 0) {
+      const KernelInfo ki = info_for(T.fn);
+      std::snprintf(buf, (size_t)buf_len,
+                    "kernel=tcgen05 grid=%d block=%d heads/block=1 tokens/stage=%d stages=%d stage_bytes=%u "
+                    "smem=%u tmem_cols=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d merge=%s",
+                    T.blocks, kTcThreads, kTcTokens, T.p.stages, T.p.stage_bytes, T.p.smem_total, T.p.tmem_cols,
+                    T.p.chunk, T.p.splits, T.occupancy, ki.regs, T.p.final_out,
+                    T.p.final_out ? "none" : T.p.merge_in_kernel ? "in-kernel" : "kernel");
+    }
+    return cudaSuccess;
+  }
   Launch L;
   e = plan_launch(a, sh, L);
   if (e != cudaSuccess) return e;
   if (buf && buf_len > 0) {
     const KernelInfo ki = info_for(L.fn);
     std::snprintf(buf, (size_t)buf_len,
-                  "grid=%d block=%d heads/block=%d tokens/stage=%d stages=%d stage_bytes=%u "
+                  "kernel=mma.sync grid=%d block=%d heads/block=%d tokens/stage=%d stages=%d stage_bytes=%u "
                   "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d",
                   L.blocks, L.threads, L.p.hh, L.p.tb, L.p.stages, L.p.stage_bytes, L.p.smem_total,
                   L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out);
@@ -355,9 +503,18 @@ extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, in
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
   }
   cudaGetLastError();
-  const int hh = heads_per_block(Hkv, fmt, d);
+  Shape shq;
+  shq.fmt = fmt;
+  shq.d = d;
+  shq.ord = 0;
+  shq.paged = paged ? 1 : 0;
+  shq.bt = paged ? block_tokens : 0;
+  shq.gpr = fmt ? d / std::max(group, 1) : 0;
+  const bool tc = group_ok(fmt, d, group) && H / Hkv <= 8 && tc_applies(shq, B * Hkv);
+  // Work units (blocks per split) and tokens per stage of the kernel that runs.
+  const int hh = tc ? 1 : heads_per_block(Hkv, fmt, d);
   const int units = B * (Hkv / hh);
-  const int tb = 16 * stage_mtiles(fmt, d);
+  const int tb = tc ? kTcTokens : 16 * stage_mtiles(fmt, d);
   int gran = tb;
   if (paged && block_tokens > tb) gran = block_tokens;
   // Blocks per SM from the launch plan (registers and shared memory); 1 when
@@ -380,26 +537,32 @@ extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, in
     sh.paged = paged ? 1 : 0;
     sh.bt = paged ? block_tokens : 0;
     sh.gpr = fmt ? d / std::max(group, 1) : 0;
-    Launch L;
-    if (group_ok(fmt, d, group) && H / Hkv <= 8 && plan_launch(&a, sh, L) == cudaSuccess) occ = L.occupancy;
+    if (tc) {
+      TcLaunch T;
+      if (plan_tc(&a, sh, T) == cudaSuccess) occ = T.occupancy;
+    } else {
+      Launch L;
+      if (group_ok(fmt, d, group) && H / Hkv <= 8 && plan_launch(&a, sh, L) == cudaSuccess) occ = L.occupancy;
+    }
     cudaGetLastError();
   }
   const int slots = sms * occ;
   const int smax = std::max(1, std::min(1024, (n + gran - 1) / gran));
-  // Pick the split count whose last wave is fullest; prefer fewer splits
-  // (less merge traffic) among near-equal choices, and at least two stages
-  // of work per block unless the sequence is short.
+  // Cost model in stage times: every wave of blocks pays a fixed fill and
+  // drain of about three stages plus its share of the stages; a split count
+  // that leaves the last wave nearly empty, or that makes many short waves,
+  // loses. Ties go to fewer splits (less merge work).
+  const double stages_per_unit = std::ceil((double)n / tb);
   int best = 1;
-  double best_score = -1;
+  double best_cost = 1e300;
   for (int s = 1; s <= smax; ++s) {
     const int chunk = ((n + s - 1) / s + gran - 1) / gran * gran;
     const int used = (n + chunk - 1) / chunk;  // non-empty splits
     if (used < s) continue;
-    const double waves = (double)units * s / slots;
-    const double eff = waves / std::ceil(waves);
-    const double score = eff - 0.0005 * s - (chunk < 2 * tb && s > 1 ? 0.5 : 0.0);
-    if (score > best_score + 1e-9) {
-      best_score = score;
+    const double waves = std::ceil((double)units * s / slots);
+    const double cost = waves * (3.0 + std::ceil(stages_per_unit / s)) * (1.0 + 0.002 * s);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
       best = s;
     }
   }

@@ -1,0 +1,735 @@
+// decode_tc.cuh - the tcgen05 (5th-generation tensor core) decode kernel for
+// int8 K/V rows of 128 dimensions.
+//
+// Counterpart of decode_partial<FMT_INT8, 128, G, U, ORD, PAGED, FINAL> in the
+// reference (runtime/kvf_kernels.cuh:124-285). One block owns a chunk of one
+// sequence's tokens for one KV head and all of its query heads; stages of 128
+// tokens stream through a TMA-fed shared-memory ring.
+//
+// Both products run on the tensor cores as exact integer MMAs
+// (tcgen05.mma kind::i8, s32 accumulators in tensor memory):
+//
+//   scores  S^T[128 tokens x cols] = K codes (u8, K-major, the TMA tile as it
+//           landed) * Q planes (s8). The query row of each head is scaled by a
+//           power of two 2^eq and rounded to a 22-bit integer Qi, written as
+//           three balanced base-256 digits (Qi = b0 + 256 b1 + 65536 b2); each
+//           digit plane is one column, and each quantization group of the row
+//           accumulates into its own columns. A token's score is then
+//             s = 2^-eq sum_g scale_g (D0 + 256 D1 + 65536 D2)_g + sum_g zero_g qsum_g
+//           with every D exact in int32 (runtime/kvf_kernels.cuh:211 dequantises
+//           the same way: scale * code + zero).
+//
+//   values  O^T[128 dims x cols] = V codes (u8, read MN-major from the same
+//           tile) * P' planes (u8), where P'_t = rint(p_t * vscale_t * 2^ev) is a
+//           24-bit integer per (token, head, group) split into three byte planes;
+//           ev puts the stage's largest V scale in [2^23, 2^24). Each stage's
+//           exact product is folded into fp32 registers with the stage's
+//           rescale. The zero term sum_t p_t * vzero_t stays on the CUDA cores.
+//
+// Warp roles (320 threads, two blocks per SM):
+//   warps 0-7  warp w serves tensor-memory lanes 32(w%4) .. 32(w%4)+31 and half
+//              w/4 of the query heads: each thread owns one token (scores) and
+//              one dimension (output) for its heads. It reads the stage's
+//              scores from tensor memory, runs the online softmax in the log2
+//              domain with one rescale per stage, writes P' planes, and folds
+//              each stage's value product into fp32;
+//   warp 8     producer: TMA for the K and V tiles, cp.async for the per-row
+//              quantization metadata of the same tokens (counted on the same
+//              full barrier);
+//   warp 9     MMA issuer (one thread): issues each stage's score MMAs as soon
+//              as its tiles land and each stage's value MMAs as soon as its P'
+//              planes are written, whichever comes first.
+// Columns of a quantization group g are ordered g*NS + half*NS/2 + plane*NH/2 +
+// head-in-half, so each warp reads and writes only its own columns.
+// With a split-counter array (kvf_args::split_sem) the last block to finish a
+// (sequence, KV head) merges that head's split partials itself
+// (decode_merge, runtime/kvf_kernels.cuh:288-306), so no second kernel runs.
+// Every wait is bounded in time; tensor memory is released before exit.
+#pragma once
+
+#include "decode_kernel.cuh"
+#include "tc.cuh"
+
+namespace kvfb {
+
+// Host-computed constants of a tensor-core launch; byte offsets relative to
+// the 1024-aligned dynamic shared-memory base.
+struct TcPlan {
+  int gq;          // query heads per KV head (<= 8)
+  int tbox;        // tokens per TMA box (128, or the page size)
+  int tbox_shift;
+  int npg;         // TMA boxes per stage: 128 / tbox
+  int stages;      // ring depth (<= 8)
+  int chunk;       // tokens per split (multiple of 128)
+  int splits;
+  int paged, tm, bt_shift;
+  int final_out;
+  int merge_in_kernel;   // split_sem given and the merge scratch fits in the ring
+  uint32_t stage_bytes;  // K tile, V tile (128 x 128 bytes each), K meta, V meta; 1024-aligned
+  uint32_t meta_bytes;   // one metadata area: 128 rows x groups x 4 bytes, 128-aligned
+  uint32_t off_q;        // Q plane tile: NS rows x 128 bytes, 128-byte swizzle
+  uint32_t off_p;        // P' tile (value MMA operand)
+  uint32_t ptile_bytes;
+  uint32_t off_misc;     // scalars, exchange areas, barriers
+  uint32_t tmem_cols;    // allocated tensor-memory columns
+  uint32_t smem_total;
+};
+
+constexpr int kTcTokens = 128;  // tokens per stage (M of the score MMA)
+constexpr int kTcThreads = 320;
+
+// Scalars, exchange areas and barriers in the misc region.
+template <int GPR, int NH> struct TcMisc {
+  float qinv[NH];             // 2^-eq per query head
+  float qsum[NH][GPR];        // 2^-eq * sum of Qi over each group
+  float red[2][8][NH / 2 + 1];  // per-warp stage maxima (+ V-scale bits), double-buffered
+  float xl[8][NH / 2];        // epilogue: per-warp sums of p
+  float xz[8][NH / 2][GPR];   // epilogue: per-warp sums of p * vzero
+  uint32_t tmem_base;
+  int abort_flag;             // set by any warp that gave up; the others stop waiting
+  int last;                   // this block is the last of its (sequence, KV head)
+  // full[8], empty[8], sfull[2], sfree[2], pready, ofull, red[2], done
+  uint64_t bars[32];
+};
+
+// Exact int -> float for the tensor-memory sums: the integer is added to the
+// bit pattern of a power-of-two float whose ulp is 1 and the power is
+// subtracted again. s22f: |v| < 2^22 (score planes), u23f: v < 2^23 (value
+// planes).
+__device__ __forceinline__ float s22f(uint32_t v) { return __int_as_float(0x4B400000 + (int)v) - 12582912.f; }
+__device__ __forceinline__ float u23f(uint32_t v) { return __uint_as_float(0x4B000000u + v) - 8388608.f; }
+
+template <int GPR, int NH>
+__global__ void __launch_bounds__(kTcThreads, 2)
+decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUtensorMap tmk,
+                 const __grid_constant__ CUtensorMap tmv) {
+  constexpr int D = 128;
+  constexpr int TB = kTcTokens;
+  constexpr int NS = NH == 4 ? 16 : 32;  // columns per group: 3 planes x NH heads, padded
+  constexpr int SC = GPR * NS;           // score columns per S buffer
+  constexpr int NP = GPR * NS;           // value columns
+  constexpr int KPG = (D / 32) / GPR;    // 32-byte k-steps per quantization group
+  constexpr int HT = NH / 2;             // query heads per thread
+  constexpr int CH = NS / 2;             // columns per half of a group
+  static_assert(NH == 4 || NH == 8, "head slots");
+  static_assert(GPR == 1 || GPR == 2, "groups per row");
+
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  TcMisc<GPR, NH> &ms = *reinterpret_cast<TcMisc<GPR, NH> *>(smem + p.off_misc);
+  volatile int *abort_flag = &ms.abort_flag;
+  const uint32_t bars = ptx::smem_u32(&ms.bars[0]);
+  const uint32_t bar_full = bars, bar_empty = bars + 64, bar_sfull = bars + 128, bar_sfree = bars + 144,
+                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 176, bar_done = bars + 192;
+  const uint32_t sq = sbase + p.off_q;
+  const uint32_t sp = sbase + p.off_p;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
+
+  const int split = blockIdx.x % p.splits;
+  const int rest = blockIdx.x / p.splits;
+  const int h = rest % a.Hkv;
+  const int b = rest / a.Hkv;
+  int nb = a.n;
+  if (a.seq_lens) nb = min(max(a.seq_lens[b], 0), a.n);
+  const int t0 = split * p.chunk;
+  const int t1 = min(nb, t0 + p.chunk);
+  const int ntiles = t1 > t0 ? (t1 - t0 + TB - 1) / TB : 0;
+
+  if (tid == 0) {
+    ms.abort_flag = 0;
+    for (int s = 0; s < p.stages; ++s) {
+      ptx::mbar_init(bar_full + 8u * s, 33u);  // expect_tx arrival + 32 cp.async arrivals
+      ptx::mbar_init(bar_empty + 8u * s, 1u);
+    }
+    for (int j = 0; j < 2; ++j) {
+      ptx::mbar_init(bar_sfull + 8u * j, 1u);
+      ptx::mbar_init(bar_sfree + 8u * j, 8u);
+      ptx::mbar_init(bar_red + 8u * j, 8u);
+    }
+    ptx::mbar_init(bar_pready, 8u);
+    ptx::mbar_init(bar_ofull, 1u);
+    ptx::mbar_init(bar_done, 1u);
+    ptx::fence_barrier_init();
+  }
+  if (warp == 9) {
+    tc::alloc(ptx::smem_u32(&ms.tmem_base), p.tmem_cols);
+    tc::relinquish();
+  }
+
+  // Q planes (warps 0-7): warp w builds head w; lane i covers dimensions
+  // 4i .. 4i+3.
+  if (warp < 8) {
+    for (int r = tid; r < NS * 8; r += 256)  // zero the whole tile (padding rows)
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(sq + 16u * r), "r"(0) : "memory");
+  }
+  __syncthreads();
+  if (warp < NH) {
+    {
+      const int hq = warp;
+      const bool live = hq < p.gq;
+      float x[4];
+      float mx = 0.f;
+      const float *qh = a.q + ((long long)b * a.H + (long long)h * p.gq + (live ? hq : 0)) * D + 4 * lane;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[j] = live ? __ldg(qh + j) * a.scale_log2 : 0.f;
+        mx = fmaxf(mx, fabsf(x[j]));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const int eq = max(min(norm_exp(mx, 22), 120), -120);
+      const float fq = eq >= 0 ? exp2i(min(eq, 127)) : exp2i(max(eq, -126));
+      uint32_t w0 = 0, w1 = 0, w2 = 0;
+      int qsum = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int qi = __float2int_rn(x[j] * fq);
+        qsum += qi;
+        const int b0 = (qi << 24) >> 24;
+        const int r1 = (qi - b0) >> 8;
+        const int b1 = (r1 << 24) >> 24;
+        const int b2 = (r1 - b1) >> 8;
+        w0 |= (uint32_t)(b0 & 255) << (8 * j);
+        w1 |= (uint32_t)(b1 & 255) << (8 * j);
+        w2 |= (uint32_t)(b2 & 255) << (8 * j);
+      }
+      // Row r of the tile at r*128 + (byte ^ ((r & 7) << 4)) (128-byte swizzle).
+      const uint32_t byte = 4u * lane;
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) {
+        const uint32_t r = (uint32_t)((hq / HT) * CH + pl * HT + (hq % HT));
+        const uint32_t ad = sq + r * 128u + (byte ^ ((r & 7u) << 4));
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ad), "r"(pl == 0 ? w0 : pl == 1 ? w1 : w2) : "memory");
+      }
+      // Group sums: GPR groups of 128/GPR dimensions = 32/GPR lanes each.
+      float gs = (float)qsum;
+#pragma unroll
+      for (int off = 1; off < 32 / GPR; off <<= 1) gs += __shfl_xor_sync(0xffffffffu, gs, off);
+      const float qinv = eq <= 0 ? exp2i(min(-eq, 127)) : exp2i(max(-eq, -126));
+      if ((lane & (32 / GPR - 1)) == 0) ms.qsum[hq][lane / (32 / GPR)] = live ? gs * qinv : 0.f;
+      if (lane == 0) ms.qinv[hq] = live ? qinv : 0.f;
+    }
+    ptx::fence_proxy_async_smem();  // the tile is read by the tensor cores
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tbase = ms.tmem_base;
+  // The separate merge kernel (if any) may be scheduled now; it waits for this grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tmk);
+      ptx::prefetch_tmap(&tmv);
+    }
+    const uint64_t pol = ptx::policy_evict_first();
+    const int tbs = p.tbox_shift;
+    const int bmask = (1 << p.bt_shift) - 1;
+    const int nblk_valid = p.paged ? min(a.max_blocks, (nb + bmask) >> p.bt_shift) : 0;
+    const long long tab0 = (long long)b * a.max_blocks;
+    int win = p.paged ? (t0 >> p.bt_shift) : 0;
+    int pg_cur = 0, pg_nxt = 0;
+    if (p.paged) {
+      if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
+      if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
+    }
+    bool ok = true;
+    int issued = 0;
+    int s = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      if (i >= p.stages && !warp_wait(bar_empty + 8u * s, phase ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const int tt = t0 + i * TB;
+      const uint32_t sk = sbase + s * p.stage_bytes;
+      const uint32_t sv = sk + TB * 128u;
+      int lanepage = 0;  // page of TMA box `lane` of this stage
+      if (p.paged) {
+        for (int j = 0; j < p.npg; ++j) {
+          const int blk = (tt + (j << tbs)) >> p.bt_shift;
+          while (blk >= win + 32) {
+            win += 32;
+            pg_cur = pg_nxt;
+            pg_nxt = (win + 32 + lane < nblk_valid) ? __ldg(a.block_table + tab0 + win + 32 + lane) : 0;
+          }
+          const int pg = __shfl_sync(0xffffffffu, pg_cur, blk - win);
+          if (lane == j) lanepage = pg;
+        }
+      }
+      if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, 2u * TB * 128u);
+      for (int j = 0; j < p.npg; ++j) {
+        const int pg = __shfl_sync(0xffffffffu, lanepage, j);
+        if (lane == 0) {
+          const int tok = tt + (j << tbs);
+          const int c1 = p.paged ? (tok & bmask) : tok;
+          const int c3 = p.paged ? pg : b;
+          const uint32_t off = (uint32_t)j * (uint32_t)(p.tbox * 128);
+          ptx::tma_g2s_4d(sk + off, &tmk, 0, c1, h, c3, bar_full + 8u * s, pol);
+          ptx::tma_g2s_4d(sv + off, &tmv, 0, c1, h, c3, bar_full + 8u * s, pol);
+        }
+      }
+      {
+        // Metadata rows of the stage's tokens that lie inside the chunk.
+        const uint32_t *kmeta = reinterpret_cast<const uint32_t *>(a.k_meta);
+        const uint32_t *vmeta = reinterpret_cast<const uint32_t *>(a.v_meta);
+        const uint32_t smk = sv + TB * 128u;
+        const uint32_t smv = smk + p.meta_bytes;
+        for (int r = lane; r < TB; r += 32) {
+          const int tok = tt + r;
+          const int pg = p.paged ? __shfl_sync(0xffffffffu, lanepage, r >> tbs) : 0;
+          if (tok >= t1) continue;
+          long long row;
+          if (p.paged) {
+            const int tl = tok & bmask;
+            const long long base = ((long long)pg * a.Hkv) << p.bt_shift;
+            row = p.tm ? base + (long long)tl * a.Hkv + h : base + ((long long)h << p.bt_shift) + tl;
+          } else {
+            row = p.tm ? ((long long)b * a.n + tok) * a.Hkv + h : ((long long)b * a.Hkv + h) * a.n + tok;
+          }
+          const uint32_t dst = (uint32_t)(r * GPR * 4);
+          if (GPR == 1) {
+            ptx::cp_async_4(smk + dst, kmeta + row);
+            ptx::cp_async_4(smv + dst, vmeta + row);
+          } else {
+            ptx::cp_async_8(smk + dst, kmeta + row * 2);
+            ptx::cp_async_8(smv + dst, vmeta + row * 2);
+          }
+        }
+        ptx::cp_async_arrive(bar_full + 8u * s);
+      }
+      issued = i + 1;
+      if (++s == p.stages) {
+        s = 0;
+        phase ^= 1u;
+      }
+      if (*abort_flag) break;
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+    // Never leave with copies in flight: wait (bounded) for the last stages.
+    for (int i = max(0, issued - p.stages); i < issued; ++i) {
+      volatile int never = 0;
+      if (!warp_wait(bar_full + 8u * (i % p.stages), (i / p.stages) & 1, &never) && lane == 0)
+        atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_S = tc::idesc_i8(false, true, false, false, 128, NS);
+      constexpr uint32_t ID_V = tc::idesc_i8(false, false, true, true, 128, NP);
+      int ns = 0, npv = 0;  // next stage for the score / value MMAs
+      bool ok = true;
+      uint64_t t_last = ptx::globaltimer_ns();
+      while (npv < ntiles) {
+        bool progress = false;
+        if (ns < ntiles) {
+          const int s = ns % p.stages, j = ns & 1;
+          if (ptx::mbar_try_wait(bar_full + 8u * s, (uint32_t)((ns / p.stages) & 1)) &&
+              (ns < 2 || ptx::mbar_try_wait(bar_sfree + 8u * j, (uint32_t)(((ns >> 1) - 1) & 1)))) {
+            tc::fence_after();
+            const uint32_t sk = sbase + (uint32_t)s * p.stage_bytes;
+#pragma unroll
+            for (int g = 0; g < GPR; ++g)
+#pragma unroll
+              for (int kk = 0; kk < KPG; ++kk) {
+                const int ks = g * KPG + kk;
+                tc::mma_i8(tbase + (uint32_t)(j * SC + g * NS),
+                           tc::smem_desc(sk + ks * 32u, 16u, 1024u, tc::kSwizzle128),
+                           tc::smem_desc(sq + ks * 32u, 16u, 1024u, tc::kSwizzle128), ID_S, kk > 0);
+              }
+            tc::commit(bar_sfull + 8u * j);
+            ++ns;
+            progress = true;
+          }
+        }
+        if (npv < ns && ptx::mbar_try_wait(bar_pready, (uint32_t)(npv & 1))) {
+          tc::fence_after();
+          const uint32_t sv = sbase + (uint32_t)(npv % p.stages) * p.stage_bytes + TB * 128u;
+#pragma unroll
+          for (int ks = 0; ks < TB / 32; ++ks)
+            tc::mma_i8(tbase + 2u * SC, tc::smem_desc(sv + ks * 4096u, 16384u, 1024u, tc::kSwizzle128),
+                       tc::smem_desc(sp + ks * 512u, 128u, 2048u, tc::kSwizzleNone), ID_V, ks > 0);
+          tc::commit(bar_ofull);
+          tc::commit(bar_empty + 8u * (npv % p.stages));
+          ++npv;
+          progress = true;
+        }
+        const uint64_t now = ptx::globaltimer_ns();
+        if (progress) {
+          t_last = now;
+        } else if (*abort_flag || now - t_last > 2000000000ull) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) {
+        atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // Tensor memory is freed below only after every MMA issued here completed.
+      tc::commit(bar_done);
+      if (!ptx::mbar_wait(bar_done, 0u, 1000000000ull)) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax / fold warps
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;  // token of the stage / output dimension
+    const uint32_t lane_base = tbase + ((uint32_t)(32 * quarter) << 16);
+    const int gd = (row * GPR) / D;       // quantization group of this thread's dimension
+    float mrun[HT], lrun[HT], zrun[HT][GPR], ocur[HT], aocur[HT], aoprev[HT];
+#pragma unroll
+    for (int e = 0; e < HT; ++e) {
+      mrun[e] = -INFINITY;
+      lrun[e] = 0.f;
+      ocur[e] = 0.f;
+      aocur[e] = aoprev[e] = 1.f;
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) zrun[e][g] = 0.f;
+    }
+    float qinv[HT], qsum[HT][GPR];
+#pragma unroll
+    for (int e = 0; e < HT; ++e) {
+      qinv[e] = ms.qinv[half * HT + e];
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) qsum[e][g] = ms.qsum[half * HT + e][g];
+    }
+    int ev_run = 23;
+    bool ok = true;
+
+    // Loads this half's CH columns of each group from tensor memory.
+    auto ld_cols = [&](uint32_t col0, uint32_t (&r)[GPR * CH]) {
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) {
+        const uint32_t ad = lane_base + col0 + (uint32_t)(g * NS + half * CH);
+        if (CH == 8) {
+          uint32_t t8[8];
+          tc::ld8(ad, t8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) r[g * CH + e] = t8[e];
+        } else {
+          uint32_t t16[16];
+          tc::ld16(ad, t16);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) r[g * CH + e] = t16[e];
+        }
+      }
+    };
+    // Folds stage k's exact value product into the fp32 accumulators.
+    auto fold = [&](int k, const float (&ao)[HT]) -> bool {
+      if (!warp_wait(bar_ofull, (uint32_t)(k & 1), abort_flag)) return false;
+      tc::fence_after();
+      uint32_t r[CH];
+      {
+        const uint32_t ad = lane_base + 2u * SC + (uint32_t)(gd * NS + half * CH);
+        if (CH == 8) {
+          uint32_t t8[8];
+          tc::ld8(ad, t8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) r[e] = t8[e];
+        } else {
+          uint32_t t16[16];
+          tc::ld16(ad, t16);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) r[e] = t16[e];
+        }
+      }
+      tc::wait_ld();
+      tc::fence_before();
+#pragma unroll
+      for (int e = 0; e < HT; ++e) {
+        const float v = fmaf(65536.f, u23f(r[2 * HT + e]), fmaf(256.f, u23f(r[HT + e]), u23f(r[e])));
+        ocur[e] = fmaf(ocur[e], ao[e], v);
+      }
+      return true;
+    };
+
+    for (int i = 0; i < ntiles; ++i) {
+      const int j = i & 1;
+      const int tok = t0 + i * TB + row;
+      const bool valid = tok < t1;
+
+      // ---- scores of this thread's token
+      if (!warp_wait(bar_sfull + 8u * j, (uint32_t)((i >> 1) & 1), abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after();
+      uint32_t sr[GPR * CH];
+      ld_cols((uint32_t)(j * SC), sr);
+      tc::wait_ld();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_sfree + 8u * j);
+
+      // Metadata of this thread's token (rows past the chunk end hold stale
+      // words and are masked).
+      const uint32_t smk = sbase + (uint32_t)(i % p.stages) * p.stage_bytes + 2u * TB * 128u;
+      const uint32_t smv = smk + p.meta_bytes;
+      uint32_t kw[GPR], vw[GPR];
+      if (GPR == 1) {
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(kw[0]) : "r"(smk + 4u * row));
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(vw[0]) : "r"(smv + 4u * row));
+      } else {
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(kw[0]), "=r"(kw[GPR - 1]) : "r"(smk + 8u * row));
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(vw[0]), "=r"(vw[GPR - 1]) : "r"(smv + 8u * row));
+      }
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) {
+        if (!valid) kw[g] = vw[g] = 0u;
+      }
+      float ks[GPR], kz[GPR], vs[GPR], vz[GPR];
+      uint32_t vbits = 0;
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) {
+        const float2 kf = meta_sz(kw[g]), vf = meta_sz(vw[g]);
+        ks[g] = kf.x;
+        kz[g] = kf.y;
+        vs[g] = vf.x;
+        vz[g] = vf.y;
+        vbits = max(vbits, vw[g] & 0x7FFFu);  // fp16 bits of a positive scale order like the values
+      }
+      float sc[HT];
+      float red[HT + 1];
+#pragma unroll
+      for (int e = 0; e < HT; ++e) {
+        float acc = 0.f, zq = 0.f;
+#pragma unroll
+        for (int g = 0; g < GPR; ++g) {
+          const uint32_t *c = sr + g * CH;
+          const float dg = fmaf(65536.f, s22f(c[2 * HT + e]), fmaf(256.f, s22f(c[HT + e]), s22f(c[e])));
+          acc = fmaf(ks[g], dg, acc);
+          zq = fmaf(kz[g], qsum[e][g], zq);
+        }
+        sc[e] = valid ? fmaf(acc, qinv[e], zq) : -INFINITY;
+        red[e] = sc[e];
+      }
+      red[HT] = __uint_as_float(vbits);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int e = 0; e <= HT; ++e) {
+          const float o = __shfl_xor_sync(0xffffffffu, red[e], off);
+          red[e] = e < HT ? fmaxf(red[e], o) : __uint_as_float(max(__float_as_uint(red[e]), __float_as_uint(o)));
+        }
+      if (lane == 0) {
+#pragma unroll
+        for (int e = 0; e <= HT; ++e) ms.red[j][warp][e] = red[e];
+        ptx::mbar_arrive(bar_red + 8u * j);
+      }
+      if (!warp_wait(bar_red + 8u * j, (uint32_t)((i >> 1) & 1), abort_flag)) {
+        ok = false;
+        break;
+      }
+      // Head maxima over the four warps of this half; V-scale maximum over all.
+#pragma unroll
+      for (int e = 0; e < HT; ++e) {
+        float v = ms.red[j][half * 4][e];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) v = fmaxf(v, ms.red[j][half * 4 + w][e]);
+        red[e] = v;
+      }
+      uint32_t vmax = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) vmax = max(vmax, __float_as_uint(ms.red[j][w][HT]));
+
+      // ---- online softmax, one rescale per stage; P' as 24-bit integers
+      const int ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vmax)), 24), 100), -100);
+      const float fv = ev >= 0 ? exp2i(min(ev, 127)) : exp2i(max(ev, -126));
+      const float fratio = exp2i(max(min(ev - ev_run, 127), -126));
+      ev_run = ev;
+      uint32_t pint[GPR][HT];
+#pragma unroll
+      for (int e = 0; e < HT; ++e) {
+        const float m_new = fmaxf(mrun[e], red[e]);
+        const float alpha = m_new == -INFINITY ? 1.f : exp2f(mrun[e] - m_new);
+        mrun[e] = m_new;
+        const float pr = (valid && m_new != -INFINITY) ? exp2f(sc[e] - m_new) : 0.f;
+        lrun[e] = fmaf(lrun[e], alpha, pr);
+        aocur[e] = alpha * fratio;
+#pragma unroll
+        for (int g = 0; g < GPR; ++g) {
+          zrun[e][g] = fmaf(zrun[e][g], alpha, valid ? pr * vz[g] : 0.f);
+          const float pv = valid ? pr * vs[g] * fv : 0.f;
+          pint[g][e] = min(__float2uint_rn(pv), 0xFFFFFFu);
+        }
+      }
+      // Byte planes: column plane*HT + head of this half.
+      uint32_t pw[GPR][4];
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) {
+        if (HT == 2) {
+          const uint32_t p0 = pint[g][0], p1 = pint[g][HT - 1];
+          pw[g][0] = ptx::prmt(ptx::prmt(p0, p1, 0x40u), ptx::prmt(p0, p1, 0x51u), 0x5410u);
+          pw[g][1] = ptx::prmt(p0, p1, 0x3362u);
+          pw[g][2] = pw[g][3] = 0u;
+        } else {
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) {
+            const uint32_t sel = (uint32_t)pl | ((uint32_t)(4 + pl) << 4);
+            const uint32_t lo = ptx::prmt(pint[g][0], pint[g][1 % HT], sel);
+            const uint32_t hi = ptx::prmt(pint[g][2 % HT], pint[g][3 % HT], sel);
+            pw[g][pl] = ptx::prmt(lo, hi, 0x5410u);
+          }
+          pw[g][3] = 0u;
+        }
+      }
+
+      // ---- fold the previous stage's value product; after it the P' tile is
+      // free again (its value MMAs have completed).
+      if (i >= 1 && !fold(i - 1, aoprev)) {
+        ok = false;
+        break;
+      }
+
+      // ---- P' planes into the value operand tile (MN-major, 16-byte rows of
+      // 16 columns per 8-token core matrix).
+      const uint32_t rowoff = (uint32_t)(row >> 3) * 128u + (uint32_t)(row & 7) * 16u;
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) {
+        if (CH == 8) {
+          asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(sp + (uint32_t)g * 2048u + rowoff + 8u * half),
+                       "r"(pw[g][0]), "r"(pw[g][1])
+                       : "memory");
+        } else {
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sp + (uint32_t)(2 * g + half) * 2048u + rowoff),
+                       "r"(pw[g][0]), "r"(pw[g][1]), "r"(pw[g][2]), "r"(pw[g][3])
+                       : "memory");
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_pready);
+#pragma unroll
+      for (int e = 0; e < HT; ++e) aoprev[e] = aocur[e];
+    }
+    if (ok && ntiles >= 1 && !fold(ntiles - 1, aoprev)) ok = false;
+    if (!ok) {
+      if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+
+    // ------------------------------------------------------------ epilogue
+    // Token-side sums over the block, then one output column per thread.
+#pragma unroll
+    for (int e = 0; e < HT; ++e) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        lrun[e] += __shfl_xor_sync(0xffffffffu, lrun[e], off);
+#pragma unroll
+        for (int g = 0; g < GPR; ++g) zrun[e][g] += __shfl_xor_sync(0xffffffffu, zrun[e][g], off);
+      }
+      if (lane == 0) {
+        ms.xl[warp][e] = lrun[e];
+#pragma unroll
+        for (int g = 0; g < GPR; ++g) ms.xz[warp][e][g] = zrun[e][g];
+      }
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float finv = exp2i(max(min(-ev_run, 127), -126));
+    const bool failed = *abort_flag != 0;
+#pragma unroll
+    for (int e = 0; e < HT; ++e) {
+      const int hq = half * HT + e;
+      if (hq < p.gq && !failed) {
+        float L = 0.f, Z = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          L += ms.xl[half * 4 + w][e];
+          Z += ms.xz[half * 4 + w][e][gd];
+        }
+        const float val = fmaf(ocur[e], finv, Z);
+        const long long head = (long long)b * a.H + (long long)h * p.gq + hq;
+        if (p.final_out) {
+          a.out[head * D + row] = L > 0.f ? val / L : 0.f;
+        } else {
+          a.part_o[(head * p.splits + split) * D + row] = val;
+          if (row == 0) {
+            a.part_ml[(head * p.splits + split) * 2] = mrun[e];
+            a.part_ml[(head * p.splits + split) * 2 + 1] = L;
+          }
+        }
+      }
+    }
+    if (p.merge_in_kernel) {
+      // Count this split in; the block that completes the count merges the
+      // head's partials (log-sum-exp in log2 units, as decode_merge does) and
+      // resets the counter for the next launch.
+      unsigned *cnt = a.split_sem + ((long long)b * a.Hkv + h);
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (tid == 0) ms.last = atomicAdd(cnt, 1u) == (unsigned)(p.splits - 1) ? 1 : 0;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (ms.last) {
+        __threadfence();
+        const int S = p.splits;
+        // Split weights 2^(m_s - M) and the merged denominator per query head,
+        // one warp per head, into the (idle) stage ring: W[hq][s], Lsum[hq].
+        float *W = reinterpret_cast<float *>(smem);
+        float *Lsum = W + 8 * S;
+        if (warp < p.gq) {
+          const long long head = (long long)b * a.H + (long long)h * p.gq + warp;
+          const float *ml = a.part_ml + head * S * 2;
+          float M = -INFINITY;
+          for (int sp = lane; sp < S; sp += 32) M = fmaxf(M, __ldcg(ml + 2 * sp));
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+          float L = 0.f;
+          for (int sp = lane; sp < S; sp += 32) {
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + sp);
+            const float wgt = (M == -INFINITY || v.x == -INFINITY) ? 0.f : exp2f(v.x - M);
+            W[warp * S + sp] = wgt;
+            L = fmaf(v.y, wgt, L);
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+          if (lane == 0) Lsum[warp] = L;
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        // out[d] = sum_s o_s[d] W[s] / L for this thread's column and heads;
+        // loads issued in batches of 16 independent ones.
+#pragma unroll
+        for (int e = 0; e < HT; ++e) {
+          const int hq = half * HT + e;
+          if (hq >= p.gq) continue;
+          const long long head = (long long)b * a.H + (long long)h * p.gq + hq;
+          const float *po = a.part_o + head * (long long)S * D + row;
+          const float *wq = W + hq * S;
+          float O = 0.f;
+          int sp = 0;
+          for (; sp + 16 <= S; sp += 16) {
+            float os[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) os[u] = __ldcg(po + (long long)(sp + u) * D);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) O = fmaf(os[u], wq[sp + u], O);
+          }
+          for (; sp < S; ++sp) O = fmaf(__ldcg(po + (long long)sp * D), wq[sp], O);
+          const float L = Lsum[hq];
+          a.out[head * D + row] = L > 0.f ? O / L : 0.f;
+        }
+        if (tid == 0) *cnt = 0u;
+      }
+    }
+    tc::fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 9) {
+    tc::fence_after();
+    tc::dealloc(tbase, p.tmem_cols);
+  }
+}
+
+} // namespace kvfb

@@ -48,13 +48,13 @@ def edge_inputs(shape, seed):
     return q, K, V
 
 
-def run(q, K, V, fmt, group, place, splits, seq_lens=None, variant=None, device="cuda:0"):
+def run(q, K, V, fmt, group, place, splits, seq_lens=None, variant=None, device="cuda:0", fused=True):
     qd = torch.as_tensor(q, device=device)
     Kd = torch.as_tensor(K, device=device)
     Vd = torch.as_tensor(V, device=device)
     cache = api.KVCache.from_logical(Kd, Vd, fmt=fmt, group=group, place=place, seq_lens=seq_lens)
     out = torch.full_like(qd, float("nan"))
-    ws = api.Workspace.allocate(q.shape[0], q.shape[1], q.shape[2], splits, qd.device)
+    ws = api.Workspace.allocate(q.shape[0], q.shape[1], q.shape[2], splits, qd.device, fused=fused)
     if variant is None:
         api.decode(qd, cache, out=out, workspace=ws)
     else:
@@ -64,6 +64,28 @@ def run(q, K, V, fmt, group, place, splits, seq_lens=None, variant=None, device=
                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
     return out.cpu().numpy()
+
+
+INT8_128 = {"f16": False, "int8": True, "int4": False}
+
+
+@pytest.fixture(params=["auto", "tcgen05", "mma.sync"])
+def kernel_path(request, monkeypatch):
+    """Runs a test on the default kernel choice and on each int8 kernel forced:
+    KVF_B200_TC=1 selects the tcgen05 kernel wherever it applies (int8 rows of
+    128 dimensions), KVF_B200_TC=0 the mma.sync kernels."""
+    env = {"auto": None, "tcgen05": "1", "mma.sync": "0"}[request.param]
+    if env is None:
+        monkeypatch.delenv("KVF_B200_TC", raising=False)
+    else:
+        monkeypatch.setenv("KVF_B200_TC", env)
+    return request.param
+
+
+def skip_if_path_irrelevant(kernel_path, fmt, d):
+    """The forced variants only differ from "auto" for int8 rows of 128."""
+    if kernel_path != "auto" and not (fmt == FMT_INT8 and d == 128):
+        pytest.skip("kernel choice applies to int8, d=128 only")
 
 
 @pytest.fixture(scope="module")
@@ -113,7 +135,7 @@ def _variant_id(r):
 
 
 @pytest.mark.parametrize("shape_name", list(EDGE_SHAPES))
-def test_reference_edge_plans(cuda, afix, shape_name):
+def test_reference_edge_plans(cuda, afix, shape_name, kernel_path):
     """Every plan the reference verified for this edge shape, by variant id."""
     shape = EDGE_SHAPES[shape_name]
     q, K, V = edge_inputs(shape, int(afix[f"{shape_name}/seed"][0]))
@@ -146,8 +168,9 @@ def _oracle_for(w, q, K, V, seq_lens, b_sel=None):
 
 
 @pytest.mark.parametrize("name", workloads.CONFIG_ORDER)
-def test_config_parity(cuda, name):
+def test_config_parity(cuda, name, kernel_path):
     w = workloads.CONFIGS[name]
+    skip_if_path_irrelevant(kernel_path, w.fmt, w.d)
     qd, Kd, Vd, seq_lens = workloads.generate(w, cuda)
     cache = api.KVCache.from_logical(Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens)
     out = api.decode(qd, cache, splits=api.suggest_splits(cache, w.H))
@@ -168,7 +191,8 @@ def test_config_parity(cuda, name):
 @pytest.mark.parametrize("place", [Placement(ORD_HEAD, False, 0), Placement(ORD_TOKEN, False, 0),
                                    Placement(ORD_HEAD, True, 32), Placement(ORD_TOKEN, True, 16)],
                          ids=lambda p: p.name)
-def test_ragged_and_empty_sequences(cuda, fmt, group, place):
+def test_ragged_and_empty_sequences(cuda, fmt, group, place, kernel_path):
+    skip_if_path_irrelevant(kernel_path, fmt, 128)
     rs = np.random.RandomState(11)
     B, H, Hkv, D, n = 7, 16, 4, 128, 700
     q = rs.standard_normal((B, H, D)).astype(np.float32)
@@ -208,7 +232,7 @@ def test_nan_rows_past_sequence_end_are_ignored(cuda):
         assert_close(got, ref, f"splits={splits}")
 
 
-def test_split_count_does_not_change_the_result(cuda):
+def test_split_count_does_not_change_the_result(cuda, kernel_path):
     rs = np.random.RandomState(13)
     B, H, Hkv, D, n = 2, 32, 8, 128, 5000
     q = rs.standard_normal((B, H, D)).astype(np.float32)
@@ -218,6 +242,53 @@ def test_split_count_does_not_change_the_result(cuda):
     outs = [run(q, K, V, FMT_INT8, 64, place, s) for s in (1, 2, 5, 16, 64, 313)]
     for o in outs[1:]:
         assert np.abs(o - outs[0]).max() < 1e-5
+
+
+@pytest.mark.parametrize("fmt,group,place,d,gq", [
+    (FMT_INT8, 64, Placement(ORD_TOKEN, True, 16), 128, 4),
+    (FMT_INT8, 128, Placement(ORD_HEAD, False, 0), 128, 8),
+    (FMT_F16, 0, Placement(ORD_HEAD, False, 0), 128, 1),
+])
+def test_in_kernel_split_merge_matches_two_launch_merge(cuda, fmt, group, place, d, gq, kernel_path):
+    skip_if_path_irrelevant(kernel_path, fmt, d)
+    """With split counters the last block of each (sequence, KV head) merges
+    the partials itself; checked against the reference's two-launch scheme and
+    the oracle on ragged sequences, twice in a row (the counters must be back
+    at zero after each call)."""
+    rs = np.random.RandomState(16)
+    B, Hkv, n = 3, 4, 2500
+    H = Hkv * gq
+    q = rs.standard_normal((B, H, d)).astype(np.float32)
+    K = rs.standard_normal((B, Hkv, n, d)).astype(np.float32)
+    V = rs.standard_normal((B, Hkv, n, d)).astype(np.float32)
+    lens = np.array([2500, 700, 0], dtype=np.int32)
+    _, _, kq = O.quantize(fmt, d, group, K.reshape(-1, d))
+    _, _, vq = O.quantize(fmt, d, group, V.reshape(-1, d))
+    ref = O.attention(q, kq.reshape(K.shape), vq.reshape(V.shape), O.scale_f32(d), seq_lens=lens)
+    qd = torch.as_tensor(q, device=cuda)
+    cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                     fmt=fmt, group=group, place=place, seq_lens=lens)
+    for splits in (2, 7, 24):
+        fused_ws = api.Workspace.allocate(B, H, d, splits, cuda, fused=True)
+        for _ in range(2):
+            got = api.decode(qd, cache, workspace=fused_ws).cpu().numpy()
+            assert_close(got, ref, f"in-kernel merge, splits={splits}")
+        assert int(fused_ws.split_sem.abs().sum()) == 0
+        two = api.decode(qd, cache, workspace=api.Workspace.allocate(B, H, d, splits, cuda, fused=False))
+        assert np.abs(got - two.cpu().numpy()).max() < 1e-5, f"splits={splits}"
+    assert api.device_errors() == 0
+
+
+def test_forced_tcgen05_kernel_is_the_one_that_runs(cuda, monkeypatch):
+    rs = np.random.RandomState(17)
+    K = torch.as_tensor(rs.standard_normal((1, 8, 512, 128)).astype(np.float32), device=cuda)
+    cache = api.KVCache.from_logical(K, K, fmt=FMT_INT8, group=64, place=Placement(ORD_TOKEN, False, 0))
+    q = torch.zeros((1, 32, 128), dtype=torch.float32, device=cuda)
+    ws = api.Workspace.allocate(1, 32, 128, 4, cuda)
+    monkeypatch.setenv("KVF_B200_TC", "1")
+    assert api.describe(q, cache, ws).startswith("kernel=tcgen05")
+    monkeypatch.setenv("KVF_B200_TC", "0")
+    assert api.describe(q, cache, ws).startswith("kernel=mma.sync")
 
 
 def test_merge_entry_point_recombines_partials(cuda):
