@@ -21,8 +21,17 @@ ranks / max-over-ranks step time, in TB/s.
           unmodified into oracle/_ref), on the host cores, over disjoint
           (sequence, KV head) slices in parallel threads
 
-At N > 1 GPUs the headline workload (not sharded by the reference) runs as N
-independent replicas (weak scaling, no collective).
+At N > 1 GPUs (one process per GPU, launched by torch.distributed.run) the
+workloads the reference does not shard, the headline among them, run as N
+independent replicas (weak scaling, no collective). The two sharded
+workloads split one problem over the N GPUs (strong scaling):
+  long_gqa_b1_n65536_int4g32_hm         split-KV: each GPU decodes its token
+                                        range, one NCCL all-gather of the
+                                        (output, lse) states, merge_states kernel
+  llama3_70b_b64_n16384_int8g64_tm_p16  KV heads: each GPU owns Hkv/N KV heads of
+                                        every sequence; no exchange (the
+                                        all-gather of the outputs is timed
+                                        separately as "with_output_gather")
 """
 from __future__ import annotations
 
@@ -140,6 +149,17 @@ def barrier(world: int):
         import torch.distributed as dist
 
         dist.barrier()
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
 
 
 def max_over_ranks(x: float, world: int) -> float:
@@ -274,23 +294,64 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    qd, Kd, Vd, seq_lens = workloads.generate(w, dev, seed=w.seed + rank)
-    cache = api.KVCache.from_logical(Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens)
-    del Kd, Vd
-    torch.cuda.empty_cache()
-    splits = args.splits or api.suggest_splits(cache, w.H)
-    ws = api.Workspace.allocate(w.B, w.H, w.d, splits, dev)
-    out = torch.empty_like(qd)
-    payload = cache.payload_bytes()
-    args_blk = api.make_args(qd, cache, out, ws)
-    stream = torch.cuda.current_stream(dev)
-    sptr = ctypes.c_void_p(stream.cuda_stream)
+    sharded = world > 1 and w.shard in ("splitkv", "kvheads")
     L = lib()
     g = w.H // w.Hkv
+    stream = torch.cuda.current_stream(dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    gather_launch = None
+    if sharded:
+        from kvforge_b200 import sharding
 
-    def launch():
-        check("kvf_b200_decode", L.kvf_b200_decode(ctypes.byref(args_blk), w.fmt, w.d, g, w.place.order,
-                                                   int(w.place.paged), sptr))
+        # One global problem (same seed on every rank), sharded.
+        qd, Kd, Vd, seq_lens = workloads.generate(w, dev, seed=w.seed)
+        cls = sharding.SplitKVDecode if w.shard == "splitkv" else sharding.HeadShardedDecode
+        sh = cls(qd, Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens, world=world, rank=rank,
+                 splits=args.splits or None)
+        del Kd, Vd
+        torch.cuda.empty_cache()
+        cache, ws, splits = sh.cache, sh.ws, sh.ws.splits
+        qd = sh.q
+        out = sh.out if w.shard == "splitkv" else sh.out_local
+        payload = cache.payload_bytes()
+
+        def launch():
+            sh.step()
+
+        if w.shard == "kvheads":
+            def gather_launch():
+                sh.step(gather=True)
+
+        def api_step():
+            sh.step()
+
+        parallelism = (f"split-KV over {world} GPUs: NCCL all-gather of (out, lse) + merge_states kernel"
+                       if w.shard == "splitkv" else f"KV heads over {world} GPUs ({w.Hkv // world} each), no exchange")
+        scaling = "strong"
+        launches_per_step = (1 if splits <= 1 or ws.split_sem is not None else 2) + (1 if w.shard == "splitkv" else 0)
+    else:
+        qd, Kd, Vd, seq_lens = workloads.generate(w, dev, seed=w.seed + rank)
+        cache = api.KVCache.from_logical(Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens)
+        del Kd, Vd
+        torch.cuda.empty_cache()
+        splits = args.splits or api.suggest_splits(cache, w.H)
+        ws = api.Workspace.allocate(w.B, w.H, w.d, splits, dev)
+        out = torch.empty_like(qd)
+        payload = cache.payload_bytes()
+        args_blk = api.make_args(qd, cache, out, ws)
+
+        def launch():
+            check("kvf_b200_decode", L.kvf_b200_decode(ctypes.byref(args_blk), w.fmt, w.d, g, w.place.order,
+                                                       int(w.place.paged), sptr))
+
+        def api_step():
+            api.decode(qd, cache, out=out, workspace=ws)
+
+        parallelism = f"{world} independent replicas" if world > 1 else "1 GPU"
+        scaling = "weak"
+        desc = api.describe(qd, cache, ws)
+        merge_in_kernel = "merge=in-kernel" in desc
+        launches_per_step = 1 if splits <= 1 or merge_in_kernel else 2
 
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     flush = torch.empty(max(96 << 20, 3 * l2), dtype=torch.uint8, device=dev)
@@ -318,6 +379,25 @@ def main():
     ms_all = max_over_ranks(ms, world)
     errs = api.device_errors()
 
+    # ---- with the output all-gather (KV-head sharding only)
+    gather_ms = None
+    if gather_launch is not None:
+        evg = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for i in range(args.warmup):
+            flush.fill_(i & 0xFF)
+            gather_launch()
+        torch.cuda.synchronize()
+        barrier(world)
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            evg[i][0].record(stream)
+            gather_launch()
+            evg[i][1].record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        gather_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evg), world)
+
     # ---- end to end through the public API, host buffers
     q_host = qd.cpu().pin_memory()
     out_host = torch.empty_like(out, device="cpu").pin_memory()
@@ -325,7 +405,7 @@ def main():
     for i in range(args.warmup):
         flush.fill_(i & 0xFF)
         qd.copy_(q_host, non_blocking=True)
-        api.decode(qd, cache, out=out, workspace=ws)
+        api_step()
         out_host.copy_(out, non_blocking=True)
     torch.cuda.synchronize()
     barrier(world)
@@ -333,14 +413,14 @@ def main():
         flush.fill_(i & 0xFF)
         ev2[i][0].record(stream)
         qd.copy_(q_host, non_blocking=True)
-        api.decode(qd, cache, out=out, workspace=ws)
+        api_step()
         out_host.copy_(out, non_blocking=True)
         ev2[i][1].record(stream)
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev2), world)
 
-    total_payload = payload * world
+    total_payload = int(sum_over_ranks(float(payload), world))
     value = total_payload / (ms_all * 1e-3) / 1e12
     peaks = measured_peaks()
     achieved_gbs = payload / (ms * 1e-3) / 1e9
@@ -348,18 +428,18 @@ def main():
     prof = ROOT / "profiles" / f"{wname}.traffic.json"
     if prof.exists():
         traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
-    launches_per_step = 2 if splits > 1 else 1
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_all, "us_per_step": ms_all * 1e3,
-            "us_per_step_median": ms_med * 1e3, "higher_is_better": True, "scaling": "weak",
+            "us_per_step_median": ms_med * 1e3, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": {0: "f16 KV", 1: "int8 KV", 2: "int4 KV"}[w.fmt] + ", fp32 accumulate",
             "data": "synthetic (seeded N(0,1) on device)",
             "config": w.config() | {"splits": splits, "payload_bytes_per_gpu": payload,
+                                    "payload_bytes_total": total_payload,
                                     "l2": "flushed before every step (3 x L2 write)",
-                                    "parallelism": "replicas" if world > 1 else "1 GPU"},
+                                    "parallelism": parallelism},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
                          "peak_source": peaks["source"] + " copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
@@ -367,9 +447,14 @@ def main():
             "e2e": {"value": total_payload / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s", "us_per_step": e2e_ms * 1e3,
                     "h2d_bytes_per_step": qd.numel() * 4, "d2h_bytes_per_step": out.numel() * 4},
             "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_note": "our kernels per timed region (decode, merge when not in-kernel, merge_states); "
+                                 "NCCL kernels not counted",
             "clocks": clk.record(),
             "device_errors": errs,
         }
+        if gather_ms is not None:
+            line["with_output_gather"] = {"us_per_step": gather_ms * 1e3,
+                                          "value": total_payload / (gather_ms * 1e-3) / 1e12, "unit": "TB/s"}
         if world == 1 and args.cpu_sample_s > 0:
             line["cpu_baseline"] = cpu_baseline(w, args.cpu_sample_s)
         print(json.dumps(line), flush=True)

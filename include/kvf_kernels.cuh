@@ -4,7 +4,7 @@
 // Keeps the names generated code and the host runtime use:
 //   kvf::Fmt / kvf::Ord enums            (runtime/kvf_kernels.cuh:26-27)
 //   kvf::Args                            (runtime/kvf_kernels.cuh:29-46), same
-//                                        field order, plus a trailing seq_lens
+//                                        field order, plus trailing seq_lens, split_sem, lse
 //   kvf::launch<FMT, D, G, U, ORD, PAGED>(const Args &, cudaStream_t)
 //                                        (runtime/kvf_kernels.cuh:309-320)
 // so that the launchers src/codegen.cpp emits (`kvf_launch_<name>`), the
@@ -46,12 +46,14 @@ struct Args {
   float scale_log2;            // softmax scale * log2(e)
   const int *seq_lens;         // [B] tokens per sequence; nullptr = n for all
   unsigned *split_sem;         // [B][Hkv] zeroed counters for the in-kernel merge; nullptr = two launches
+  float *lse;                  // [B][H] log2 softmax denominators, optional
 };
 
 static_assert(sizeof(Args) == sizeof(kvf_args), "kvf::Args must mirror kvf_args");
 static_assert(offsetof(Args, scale_log2) == offsetof(kvf_args, scale_log2), "layout");
 static_assert(offsetof(Args, seq_lens) == offsetof(kvf_args, seq_lens), "layout");
 static_assert(offsetof(Args, split_sem) == offsetof(kvf_args, split_sem), "layout");
+static_assert(offsetof(Args, lse) == offsetof(kvf_args, lse), "layout");
 
 inline const kvf_args *c_args(const Args &a) { return reinterpret_cast<const kvf_args *>(&a); }
 

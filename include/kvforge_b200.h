@@ -59,6 +59,11 @@ enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
  *                runs; part_o/part_ml are still written and read. NULL = the
  *                reference's two-launch scheme. Calls sharing one array must
  *                not overlap on the GPU.
+ *   lse          [B][H] fp32, optional (NULL = not written): log2 of the
+ *                softmax denominator of each query head, in the same units as
+ *                part_ml (max + log2(sum)); -inf for a head with no tokens.
+ *                It lets outputs computed on different token ranges (e.g. on
+ *                different GPUs) be combined with kvf_b200_merge_states.
  */
 typedef struct kvf_args {
   const float *q;
@@ -80,6 +85,7 @@ typedef struct kvf_args {
   /* ---- additions (zero = reference behaviour) ---- */
   const int *seq_lens;
   unsigned *split_sem;
+  float *lse;
 } kvf_args;
 
 /* One decode step: the sm_100a counterpart of
@@ -100,6 +106,19 @@ cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, i
 /* The split merge alone (decode_merge<D>, runtime/kvf_kernels.cuh:288-306):
  * out[b][h] = sum_s part_o[s] * 2^(m_s - M) / sum_s l_s * 2^(m_s - M). */
 cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream);
+
+/* Combines attention outputs of the same query heads computed over disjoint
+ * token ranges (e.g. one range per GPU when the KV cache is split across
+ * GPUs along the tokens):
+ *   out[i][x] = sum_p 2^(lse_p[i] - LSE) * o_p[i][x],   LSE = log2 sum_p 2^lse_p[i]
+ * Part p's normalised output o_p [rows][d] starts at o + p * o_stride and its
+ * lse_p [rows] (as written by kvf_b200_decode through kvf_args::lse) at
+ * lse + p * lse_stride (strides in floats), so parts gathered into one packed
+ * buffer per rank need no copy. out [rows][d]; lse_out [rows] (NULL = not
+ * written) receives LSE. A row whose parts all have lse = -inf gets zeros.
+ * No reference counterpart: the reference runs on one GPU. */
+cudaError_t kvf_b200_merge_states(const float *o, const float *lse, int P, int rows, int d, long long o_stride,
+                                  long long lse_stride, float *out, float *lse_out, cudaStream_t stream);
 
 /* Launch by variant id, e.g. "int8_tm_p_g4_u2_d128": the registry lookup plus
  * call of bench/sweep.cu:180-184 (id format of src/codegen.cpp:59-65,

@@ -20,7 +20,7 @@ FMT_NAMES = {"f16": FMT_F16, "int8": FMT_INT8, "int4": FMT_INT4}
 
 class KvfArgs(ctypes.Structure):
     """Mirror of kvf_args / kvf::Args (runtime/kvf_kernels.cuh:29-46) plus the
-    appended seq_lens and split_sem fields."""
+    appended seq_lens, split_sem and lse fields."""
 
     _fields_ = [
         ("q", c_void_p),
@@ -44,6 +44,7 @@ class KvfArgs(ctypes.Structure):
         ("scale_log2", c_float),
         ("seq_lens", c_void_p),
         ("split_sem", c_void_p),
+        ("lse", c_void_p),
     ]
 
 
@@ -71,6 +72,8 @@ _lib = None
 SIGNATURES = [
     ("kvf_b200_decode", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_merge", c_int, [ctypes.POINTER(KvfArgs), c_int, c_void_p]),
+    ("kvf_b200_merge_states", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_longlong,
+                                       ctypes.c_longlong, c_void_p, c_void_p, c_void_p]),
     ("kvf_b200_decode_noalloc", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_launch_variant", c_int, [c_char_p, ctypes.POINTER(KvfArgs), c_void_p]),
     ("kvf_b200_variant_count", c_int, []),

@@ -192,10 +192,13 @@ def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace)
 
 def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = None,
            splits: Optional[int] = None, workspace: Optional[Workspace] = None, stream=None,
-           g: int = 1) -> torch.Tensor:
+           g: int = 1, lse: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One decode step: out[b][h] = softmax(q k^T * scale) v over the cache.
 
-    q: float32 [B][H][D] on the cache's device. Returns out (float32 [B][H][D])."""
+    q: float32 [B][H][D] on the cache's device. Returns out (float32 [B][H][D]).
+    lse (optional float32 [B][H]) receives log2 of each head's softmax
+    denominator, for combining outputs over disjoint token ranges with
+    merge_states."""
     if q.dtype != torch.float32 or not q.is_contiguous():
         raise ValueError("q must be a contiguous float32 tensor [B][H][D]")
     B, H, d = q.shape
@@ -205,11 +208,36 @@ def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = Non
         s = splits if splits is not None else suggest_splits(cache, H)
         workspace = Workspace.allocate(B, H, d, s, q.device)
     a = make_args(q, cache, out, workspace)
+    if lse is not None:
+        if lse.dtype != torch.float32 or not lse.is_contiguous() or lse.numel() != B * H:
+            raise ValueError("lse must be a contiguous float32 tensor [B][H]")
+        a.lse = lse.data_ptr()
     check(
         "kvf_b200_decode",
         lib().kvf_b200_decode(ctypes.byref(a), cache.fmt, d, g, cache.place.order,
                               int(cache.place.paged), _stream(stream)),
     )
+    return out
+
+
+def merge_states(outs: torch.Tensor, lses: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+    """Combines P outputs of the same heads over disjoint token ranges:
+    outs [P][..., D] and lses [P][...] (as from decode(..., lse=...)) ->
+    [..., D], on the GPU (kvf_b200_merge_states)."""
+    if outs.dtype != torch.float32 or lses.dtype != torch.float32:
+        raise ValueError("float32 tensors expected")
+    outs = outs.contiguous()
+    lses = lses.contiguous()
+    P, d = outs.shape[0], outs.shape[-1]
+    rows = lses[0].numel()
+    if outs[0].numel() != rows * d:
+        raise ValueError("outs and lses disagree on the row count")
+    if out is None:
+        out = torch.empty(outs.shape[1:], dtype=torch.float32, device=outs.device)
+    check("kvf_b200_merge_states",
+          lib().kvf_b200_merge_states(ctypes.c_void_p(outs.data_ptr()), ctypes.c_void_p(lses.data_ptr()), P, rows,
+                                      d, rows * d, rows, ctypes.c_void_p(out.data_ptr()), None, _stream(stream)))
     return out
 
 
@@ -229,5 +257,5 @@ def device_errors() -> int:
     return int(lib().kvf_b200_device_errors())
 
 
-__all__ = ["KVCache", "Workspace", "decode", "quantize", "suggest_splits", "make_args", "describe",
+__all__ = ["KVCache", "Workspace", "decode", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
            "device_errors", "row_bytes", "groups_per_row", "scale_log2", "FMT_F16", "FMT_INT8", "FMT_INT4"]

@@ -458,6 +458,17 @@ extern "C" cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t str
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+extern "C" cudaError_t kvf_b200_merge_states(const float *o, const float *lse, int P, int rows, int d,
+                                             long long o_stride, long long lse_stride, float *out, float *lse_out,
+                                             cudaStream_t stream) {
+  if (P < 1 || rows < 0 || d < 1 || d > 1024 || !o || !lse || !out) return cudaErrorInvalidValue;
+  if (o_stride < (long long)rows * d || lse_stride < rows) return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  const int threads = (d + 31) / 32 * 32;
+  merge_states_kernel<<<rows, threads, 0, stream>>>(o, lse, P, rows, d, o_stride, lse_stride, out, lse_out);
+  return cudaGetLastError();
+}
+
 extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged,
                                          char *buf, int buf_len) {
   Shape sh;

@@ -831,6 +831,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       float *dst;
       if (p.final_out) {
         dst = a.out + head * D;
+        if (g8 == 0 && a.lse) a.lse[head] = L > 0.f ? m_run[nt] + log2f(L) : -INFINITY;
       } else {
         dst = a.part_o + (head * p.splits + split) * D;
         if (g8 == 0) {
@@ -920,7 +921,30 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args 
       }
     }
     if (colok) a.out[head * d + col] = Lt > 0.f ? Ot / Lt : 0.f;
+    if (lane == 0 && blockIdx.z == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
   }
+}
+
+// Combination of attention states over disjoint token ranges (no reference
+// counterpart): one block per output row, one thread per column; P is small
+// (one part per GPU).
+__global__ void merge_states_kernel(const float *o, const float *lse, int P, int rows, int d, long long o_stride,
+                                    long long lse_stride, float *out, float *lse_out) {
+  const int r = blockIdx.x;
+  const int c = threadIdx.x;
+  float M = -INFINITY;
+  for (int k = 0; k < P; ++k) M = fmaxf(M, __ldg(lse + k * lse_stride + r));
+  float W = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+    for (int k = 0; k < P; ++k) {
+      const float lk = __ldg(lse + k * lse_stride + r);
+      const float w = lk == -INFINITY ? 0.f : exp2f(lk - M);
+      W += w;
+      if (c < d && w > 0.f) O = fmaf(w, __ldg(o + k * o_stride + (long long)r * d + c), O);
+    }
+  }
+  if (c < d) out[(long long)r * d + c] = W > 0.f ? O / W : 0.f;
+  if (c == 0 && lse_out) lse_out[r] = W > 0.f ? M + log2f(W) : -INFINITY;
 }
 
 } // namespace kvfb

@@ -653,6 +653,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         const long long head = (long long)b * a.H + (long long)h * p.gq + hq;
         if (p.final_out) {
           a.out[head * D + row] = L > 0.f ? val / L : 0.f;
+          if (row == 0 && a.lse) a.lse[head] = L > 0.f ? mrun[e] + log2f(L) : -INFINITY;
         } else {
           a.part_o[(head * p.splits + split) * D + row] = val;
           if (row == 0) {
@@ -694,7 +695,10 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
           }
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-          if (lane == 0) Lsum[warp] = L;
+          if (lane == 0) {
+            Lsum[warp] = L;
+            if (a.lse) a.lse[head] = L > 0.f ? M + log2f(L) : -INFINITY;
+          }
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
         // out[d] = sum_s o_s[d] W[s] / L for this thread's column and heads;

@@ -117,6 +117,49 @@ def rel_l2(a: np.ndarray, ref: np.ndarray) -> float:
     return float(lib().kvfo_rel_l2(_ptr(a), _ptr(ref), a.size))
 
 
+def attention_states(q: np.ndarray, K: np.ndarray, V: np.ndarray, scale: float, seq_lens=None):
+    """(out, lse) in fp64 numpy for small cases: out as `attention`, lse[b][h]
+    = log2 sum_t 2^(q.k_t * scale * log2 e) over the valid tokens (-inf when a
+    sequence has none). The reference has no lse (it decodes on one GPU);
+    this is the quantity kvf_args::lse carries so partial outputs over
+    disjoint token ranges can be combined (see merge_states)."""
+    q = np.asarray(q, dtype=np.float64)
+    K = np.asarray(K, dtype=np.float64)
+    V = np.asarray(V, dtype=np.float64)
+    B, H, d = q.shape
+    Hkv, n = K.shape[1], K.shape[2]
+    g = H // Hkv
+    out = np.zeros((B, H, d))
+    lse = np.full((B, H), -np.inf)
+    c = scale * np.log2(np.e)
+    for b in range(B):
+        nb = n if seq_lens is None else int(seq_lens[b])
+        for h in range(H):
+            if nb <= 0:
+                continue
+            s = K[b, h // g, :nb] @ q[b, h] * c
+            m = s.max()
+            w = np.exp2(s - m)
+            out[b, h] = w @ V[b, h // g, :nb] / w.sum()
+            lse[b, h] = m + np.log2(w.sum())
+    return out.astype(np.float32), lse.astype(np.float32)
+
+
+def merge_states(outs, lses):
+    """Combination of per-part (out, lse) over disjoint token ranges, fp64:
+    out = sum_p 2^(lse_p - LSE) out_p with LSE = log2 sum_p 2^lse_p; rows
+    whose parts are all empty get zeros."""
+    outs = np.asarray(outs, dtype=np.float64)
+    lses = np.asarray(lses, dtype=np.float64)
+    M = lses.max(axis=0)
+    finite = np.isfinite(M)
+    w = np.where(np.isfinite(lses), np.exp2(lses - np.where(finite, M, 0.0)), 0.0)
+    W = w.sum(axis=0)
+    out = (w[..., None] * outs).sum(axis=0) / np.where(W > 0, W, 1.0)[..., None]
+    out[~(W > 0)] = 0.0
+    return out.astype(np.float32)
+
+
 def scale_f32(d: int) -> float:
     """1/sqrt(D) in fp32 (runtime/kvf_driver.cu:33)."""
     return float(np.float32(1.0) / np.sqrt(np.float32(d)))

@@ -72,7 +72,7 @@ def test_args_layout_matches_reference_struct(tmp_path):
     subprocess.run([gcc, f"-I{INCLUDE}", "-I/usr/local/cuda/include", str(src), "-o", str(exe)], check=True)
     out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
                                                        check=True).stdout.splitlines())
-    assert int(out["size"]) == ctypes.sizeof(KvfArgs) == 128
+    assert int(out["size"]) == ctypes.sizeof(KvfArgs) == 136
     for f in fields:
         assert int(out[f]) == getattr(KvfArgs, f).offset, f
     # The reference's prefix: 9 pointers, 9 ints, 1 float.

@@ -1,0 +1,125 @@
+"""Multi-GPU decode (kvforge_b200.sharding) on the GPU.
+
+* kvf_b200_merge_states: decoding disjoint token ranges separately (with the
+  lse output) and combining them equals one decode over all tokens, and the
+  oracle, on one GPU;
+* with two or more GPUs, two NCCL ranks run the split-KV and the KV-head
+  protocols end to end and must match a single-GPU decode of the same
+  inputs (skipped on a one-GPU box).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import assert_close
+from oracle import oracle as O
+
+torch = pytest.importorskip("torch")
+
+from kvforge_b200 import FMT_F16, FMT_INT4, FMT_INT8, ORD_HEAD, ORD_TOKEN, api, sharding  # noqa: E402
+from kvforge_b200.layout import Placement  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("fmt,group,place", [
+    (FMT_INT4, 32, Placement(ORD_HEAD, False, 0)),
+    (FMT_INT8, 64, Placement(ORD_TOKEN, True, 16)),
+    (FMT_F16, 0, Placement(ORD_TOKEN, False, 0)),
+])
+def test_merge_states_over_token_ranges_equals_one_decode(cuda, fmt, group, place):
+    rs = np.random.RandomState(41)
+    B, H, Hkv, D, n, P = 2, 32, 8, 128, 3000, 3
+    q = torch.as_tensor(rs.standard_normal((B, H, D)).astype(np.float32), device=cuda)
+    K = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    V = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    lens = np.array([3000, 1100], dtype=np.int32)
+    full = api.decode(q, api.KVCache.from_logical(K, V, fmt=fmt, group=group, place=place, seq_lens=lens))
+    outs = torch.empty((P, B, H, D), device=cuda)
+    lses = torch.empty((P, B, H), device=cuda)
+    for r in range(P):
+        t0, t1 = sharding.token_range(n, P, r)
+        ll = sharding.local_seq_lens(lens, n, t0, t1)
+        part = api.KVCache.from_logical(K[:, :, t0:t1].contiguous(), V[:, :, t0:t1].contiguous(), fmt=fmt,
+                                        group=group, place=place, seq_lens=ll)
+        api.decode(q, part, out=outs[r], lse=lses[r])
+    # the second sequence has no tokens in the last range: its lse is -inf there
+    assert torch.isinf(lses[P - 1, 1]).all()
+    merged = api.merge_states(outs, lses)
+    torch.cuda.synchronize()
+    assert (merged - full).abs().max().item() < 1e-5
+    Kn, Vn = K.cpu().numpy(), V.cpu().numpy()
+    _, _, kd = O.quantize(fmt, D, group, Kn.reshape(-1, D))
+    _, _, vd = O.quantize(fmt, D, group, Vn.reshape(-1, D))
+    ref = O.attention(q.cpu().numpy(), kd.reshape(Kn.shape), vd.reshape(Vn.shape), O.scale_f32(D), seq_lens=lens)
+    assert_close(merged.cpu().numpy(), ref, "merged")
+    assert api.device_errors() == 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(dev, kind):
+    g = torch.Generator(device=dev)
+    g.manual_seed(51)
+    if kind == "splitkv":
+        B, H, Hkv, D, n = 1, 32, 8, 128, 5000
+    else:
+        B, H, Hkv, D, n = 4, 64, 8, 128, 1500
+    q = torch.randn((B, H, D), generator=g, device=dev)
+    K = torch.randn((B, Hkv, n, D), generator=g, device=dev)
+    V = torch.randn((B, Hkv, n, D), generator=g, device=dev)
+    return q, K, V
+
+
+def _rank(rank, world, port, results):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        q, K, V = _inputs(dev, "splitkv")
+        lens = np.array([4321], dtype=np.int32)
+        sk = sharding.SplitKVDecode(q, K, V, fmt=FMT_INT4, group=32, place=Placement(ORD_HEAD, False, 0),
+                                    seq_lens=lens, world=world, rank=rank)
+        a = sk.step().cpu().numpy()
+        q, K, V = _inputs(dev, "kvheads")
+        hs = sharding.HeadShardedDecode(q, K, V, fmt=FMT_INT8, group=64, place=Placement(ORD_TOKEN, True, 16),
+                                        seq_lens=None, world=world, rank=rank)
+        b = hs.step(gather=True).cpu().numpy()
+        torch.cuda.synchronize()
+        results[rank] = (a, b, api.device_errors())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_nccl_ranks_match_one_gpu():
+    import torch.multiprocessing as mp
+
+    world = 2
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.spawn(_rank, args=(world, _free_port(), results), nprocs=world, join=True)
+        res = dict(results)
+    dev = torch.device("cuda", 0)
+    q, K, V = _inputs(dev, "splitkv")
+    ref_a = api.decode(q, api.KVCache.from_logical(K, V, fmt=FMT_INT4, group=32, place=Placement(ORD_HEAD, False, 0),
+                                                   seq_lens=np.array([4321], dtype=np.int32))).cpu().numpy()
+    q, K, V = _inputs(dev, "kvheads")
+    ref_b = api.decode(q, api.KVCache.from_logical(K, V, fmt=FMT_INT8, group=64,
+                                                   place=Placement(ORD_TOKEN, True, 16))).cpu().numpy()
+    for r in range(world):
+        a, b, errs = res[r]
+        assert errs == 0
+        assert np.abs(a - ref_a).max() < 1e-5, r
+        assert np.abs(b - ref_b).max() < 1e-6, r
