@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--workload", default=None)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--splits", type=int, default=0, help="override the split count")
+    p.add_argument("--batch", type=int, default=0,
+                   help="override the workload's batch (smaller captures for ncu); reported in config")
     p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (s)")
     return p.parse_args()
 
@@ -277,6 +279,10 @@ def main():
 
     wname = args.workload or workloads.HEADLINE
     w = workloads.CONFIGS[wname]
+    if args.batch:
+        import dataclasses
+
+        w = dataclasses.replace(w, B=args.batch)
     if args.impl == "reference":
         run_reference_arm(args, w, world, rank)
         if world > 1:
