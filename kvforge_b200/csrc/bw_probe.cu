@@ -137,11 +137,13 @@ __global__ void __launch_bounds__(32) tma_tile_stream(const __grid_constant__ CU
   }
 }
 
-// Dependent pointer chase for the idle DRAM latency.
-__global__ void chase(const unsigned *next, int steps, unsigned *out) {
-  unsigned j = 0;
+// Dependent pointer chase for the idle DRAM latency. Each run continues the
+// cycle where the previous one stopped (`pos`), so repeated runs never touch
+// a line twice and every access misses L2.
+__global__ void chase(const unsigned *next, int steps, unsigned *pos) {
+  unsigned j = *pos;
   for (int i = 0; i < steps; ++i) j = __ldcg(next + j);
-  *out = j;
+  *pos = j;
 }
 
 // L2-resident re-reads.
@@ -347,6 +349,16 @@ int main(int argc, char **argv) {
   PROBE_CHECK(cudaMalloc(&dnext, nidx * 4));
   PROBE_CHECK(cudaMalloc(&dout, 4));
   PROBE_CHECK(cudaMemcpy(dnext, nxt.data(), nidx * 4, cudaMemcpyHostToDevice));
+  PROBE_CHECK(cudaMemset(dout, 0, 4));
+  {
+    // Evict the freshly written chase lines from L2 before timing.
+    void *scratch = nullptr;
+    const size_t sb = (size_t)4 * (size_t)prop.l2CacheSize;
+    PROBE_CHECK(cudaMalloc(&scratch, sb));
+    PROBE_CHECK(cudaMemset(scratch, 1, sb));
+    PROBE_CHECK(cudaDeviceSynchronize());
+    PROBE_CHECK(cudaFree(scratch));
+  }
   const int steps = 20000;
   const float msl = tm.best_ms([&] { chase<<<1, 1>>>(dnext, steps, dout); }, 3);
   const double lat_ns = msl * 1e6 / steps;
