@@ -45,7 +45,7 @@ struct Args {
   int max_blocks;              // pages per sequence in the block table
   float scale_log2;            // softmax scale * log2(e)
   const int *seq_lens;         // [B] tokens per sequence; nullptr = n for all
-  unsigned *split_sem;         // [B][Hkv] zeroed counters for the in-kernel merge; nullptr = two launches
+  unsigned *split_sem;         // [B][Hkv][2] zeroed counters for the in-kernel merge; nullptr = two launches
   float *lse;                  // [B][H] log2 softmax denominators, optional
 };
 

@@ -136,11 +136,11 @@ class KVCache:
 class Workspace:
     """Split partials: part_o [B][H][splits][D] and part_ml [B][H][splits][2].
 
-    ``split_sem`` (zeroed uint32 counters, one per (sequence, query head),
-    enough for any Hkv <= H) lets the kernel merge the splits itself: the last
-    block to finish a (sequence, KV head) merges its partials and resets the
-    counter. ``fused=False`` leaves it out, and a separate merge kernel runs as
-    in the reference.
+    ``split_sem`` (zeroed uint32 counters, two per (sequence, query head),
+    enough for any Hkv <= H) lets the tensor-core kernel merge the splits
+    itself: the last block of a (sequence, KV head) merges and resets the
+    counters. ``fused=False`` leaves it out: a separate merge kernel, as in
+    the reference.
     """
 
     splits: int
@@ -156,7 +156,7 @@ class Workspace:
             splits,
             torch.empty((B, H, splits, d), dtype=torch.float32, device=device),
             torch.empty((B, H, splits, 2), dtype=torch.float32, device=device),
-            torch.zeros((B * H,), dtype=torch.int32, device=device) if fused else None,
+            torch.zeros((2 * B * H,), dtype=torch.int32, device=device) if fused else None,
         )
 
 

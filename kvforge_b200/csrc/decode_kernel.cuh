@@ -244,10 +244,10 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   if (a.seq_lens) nb = min(max(a.seq_lens[b], 0), a.n);
   const int t0 = split * p.chunk;
   const int t1 = min(nb, t0 + p.chunk);
-  const int ntiles = t1 > t0 ? (t1 - t0 + TB - 1) / TB : 0;
   const int tbs = p.tbox_shift;
 
   __shared__ int s_abort;
+  __shared__ int s_tag[8];  // first token of the stage in each ring slot, -1 = no more work
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < p.stages; ++s) {
@@ -270,51 +270,50 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     const int bmask = (1 << p.bt_shift) - 1;
     const int nblk_valid = p.paged ? min(a.max_blocks, (nb + bmask) >> p.bt_shift) : 0;
     const long long tab0 = (long long)b * a.max_blocks;
-    // Page ids of a 32-block window, one per lane, and of the next window.
-    int win = p.paged ? (t0 >> p.bt_shift) : 0;
-    int pg_cur = 0, pg_nxt = 0;
-    if (p.paged) {
-      if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
-      if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
-    }
     const int h0 = hgi * p.hh;
     const uint32_t *kmeta = reinterpret_cast<const uint32_t *>(a.k_meta);
     const uint32_t *vmeta = reinterpret_cast<const uint32_t *>(a.v_meta);
+    // Stages to load: the chunk [t0, t1) in TB steps; each ring slot is tagged
+    // with its first token, and a slot tagged -1 tells the consumers to stop.
+    int tt = t0;
     bool ok = true;
+    bool ended = false;
     int issued = 0;
-    for (int i = 0; i < ntiles; ++i) {
-      const int s = i % p.stages;
-      if (i >= p.stages && !warp_wait(bar_empty + 8u * s, ((i / p.stages) - 1) & 1, &s_abort)) {
+    int s = 0;
+    uint32_t phase = 0;
+    for (int i = 0;; ++i) {
+      const int cur = tt < t1 ? tt : -1;  // first token of stage i, -1 when done
+      if (i >= p.stages && !warp_wait(bar_empty + 8u * s, phase ^ 1u, &s_abort)) {
         ok = false;
         break;
       }
-      const int tt = t0 + i * TB;
+      if (cur < 0) {
+        // No more work: a slot tagged -1, completed by plain arrivals.
+        if (lane == 0) *reinterpret_cast<volatile int *>(&s_tag[s]) = -1;
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar_full + 8u * s);
+        if (GPR > 0) ptx::mbar_arrive(bar_full + 8u * s);  // 32 more: the cp.async share
+        ended = true;
+        break;
+      }
+      if (lane == 0) *reinterpret_cast<volatile int *>(&s_tag[s]) = cur;
       const uint32_t sk = sbase + s * p.stage_bytes;
       const uint32_t sv = sk + p.kv_bytes;
-      // Page of each token box of this stage (paged; at most MT boxes).
-      int pages[MT];
+      // Page of TMA box `lane` of this stage (paged).
+      int lanepage = 0;
+      if (p.paged && lane < p.npg) {
+        const int blk = (cur + (lane << tbs)) >> p.bt_shift;
+        lanepage = blk < nblk_valid ? __ldg(a.block_table + tab0 + blk) : 0;
+      }
+      if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, p.tx_bytes);
 #pragma unroll
       for (int j = 0; j < MT; ++j) {
-        pages[j] = 0;
-        if (p.paged && j < p.npg) {
-          const int blk = (tt + (j << tbs)) >> p.bt_shift;
-          while (blk >= win + 32) {
-            win += 32;
-            pg_cur = pg_nxt;
-            pg_nxt = (win + 32 + lane < nblk_valid) ? __ldg(a.block_table + tab0 + win + 32 + lane)
-                                                     : 0;
-          }
-          pages[j] = __shfl_sync(0xffffffffu, pg_cur, blk - win);
-        }
-      }
-      if (lane == 0) {
-        ptx::mbar_arrive_expect_tx(bar_full + 8u * s, p.tx_bytes);
-#pragma unroll
-        for (int j = 0; j < MT; ++j) {
-          if (j < p.npg) {
-            const int tok = tt + (j << tbs);
+        if (j < p.npg) {
+          const int pg = __shfl_sync(0xffffffffu, lanepage, j);
+          if (lane == 0) {
+            const int tok = cur + (j << tbs);
             const int c1 = p.paged ? (tok & bmask) : tok;
-            const int c3 = p.paged ? pages[j] : b;
+            const int c3 = p.paged ? pg : b;
 #pragma unroll
             for (int xb = 0; xb < RB / BOXX; ++xb) {
               const uint32_t off = (uint32_t)(xb * p.npg + j) * p.box_bytes;
@@ -325,21 +324,19 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
         }
       }
       if (GPR > 0) {
-        // Metadata rows (hh heads x TB tokens) of the tokens inside the chunk.
+        // Metadata rows (hh heads x TB tokens) of the stage's tokens.
         const uint32_t smk = sv + p.kv_bytes;
         const uint32_t smv = smk + p.meta_bytes;
-        for (int r = lane; r < p.hh * TB; r += 32) {
+        const int rows = p.hh * TB;
+        for (int r0 = 0; r0 < rows; r0 += 32) {
+          const int r = r0 + lane;
           const int hl = r / TB, t = r - hl * TB;
-          const int tok = tt + t;
-          if (tok >= t1) continue;
+          const int tok = cur + t;
+          const int pg = p.paged ? __shfl_sync(0xffffffffu, lanepage, (t >> tbs) & 31) : 0;
+          if (r >= rows || tok >= nb) continue;
           const int h = h0 + hl;
           long long row;
           if (p.paged) {
-            const int j = t >> tbs;
-            int pg = pages[0];
-#pragma unroll
-            for (int jj = 1; jj < MT; ++jj)
-              if (jj == j) pg = pages[jj];
             const int tl = tok & bmask;
             const long long base = ((long long)pg * a.Hkv) << p.bt_shift;
             row = p.tm ? base + (long long)tl * a.Hkv + h : base + ((long long)h << p.bt_shift) + tl;
@@ -361,6 +358,11 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
         ptx::cp_async_arrive(bar_full + 8u * s);
       }
       issued = i + 1;
+      tt += TB;
+      if (++s == p.stages) {
+        s = 0;
+        phase ^= 1u;
+      }
       if (s_abort) break;
     }
     if (!ok) {
@@ -368,7 +370,10 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       s_abort = 1;
     }
     // Never leave with copies in flight: wait (bounded) for the last stages.
-    for (int i = max(0, issued - p.stages); i < issued; ++i) {
+    // The end-of-work slot reused the barrier of stage issued - stages, which
+    // was consumed (and so landed) before the slot was reused; its old parity
+    // must not be waited on again.
+    for (int i = max(0, issued - p.stages + (ended ? 1 : 0)); i < issued; ++i) {
       const int s = i % p.stages;
       volatile int never = 0;
       if (!warp_wait(bar_full + 8u * s, (i / p.stages) & 1, &never) && lane == 0)
@@ -490,13 +495,14 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   int s = 0;
   uint32_t phase = 0;
   bool ok = true;
-  for (int i = 0; i < ntiles; ++i) {
+  for (;;) {
     if (!warp_wait(bar_full + 8u * s, phase, &s_abort)) {
       ok = false;
       break;
     }
-    const int tt = t0 + i * TB;
-    const int vt = min(TB, t1 - tt);  // valid tokens in this stage
+    const int tt = *reinterpret_cast<volatile int *>(&s_tag[s]);  // first token of the stage
+    if (tt < 0) break;                                               // no more work
+    const int vt = min(TB, nb - tt);  // valid tokens in this stage
     const uint32_t sk = sbase + s * p.stage_bytes;
     const uint32_t sv = sk + p.kv_bytes;
     const uint32_t smk = sv + p.kv_bytes;
@@ -807,8 +813,8 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   if (!ok) {
     if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
     s_abort = 1;
-    return;
   }
+  if (!ok) return;
   // Reduce the per-thread sums over the 8 row groups.
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {

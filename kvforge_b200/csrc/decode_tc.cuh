@@ -667,7 +667,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       // Count this split in; the block that completes the count merges the
       // head's partials (log-sum-exp in log2 units, as decode_merge does) and
       // resets the counter for the next launch.
-      unsigned *cnt = a.split_sem + ((long long)b * a.Hkv + h);
+      unsigned *cnt = a.split_sem + 2 * ((long long)b * a.Hkv + h);
       __threadfence();
       asm volatile("bar.sync 1, 256;" ::: "memory");
       if (tid == 0) ms.last = atomicAdd(cnt, 1u) == (unsigned)(p.splits - 1) ? 1 : 0;
