@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--workload", default=None)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--splits", type=int, default=0, help="override the split count")
+    p.add_argument("--exchange", default="fused", choices=["fused", "nvlink", "nccl"],
+                   help="split-KV state exchange across GPUs: fused into the split merge over NVLink, separate "
+                        "NVLink push/merge kernels, or an NCCL all-gather")
     p.add_argument("--batch", type=int, default=0,
                    help="override the workload's batch (smaller captures for ncu); reported in config")
     p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (s)")
@@ -311,9 +314,12 @@ def main():
 
         # One global problem (same seed on every rank), sharded.
         qd, Kd, Vd, seq_lens = workloads.generate(w, dev, seed=w.seed)
-        cls = sharding.SplitKVDecode if w.shard == "splitkv" else sharding.HeadShardedDecode
-        sh = cls(qd, Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens, world=world, rank=rank,
-                 splits=args.splits or None)
+        if w.shard == "splitkv":
+            sh = sharding.SplitKVDecode(qd, Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens,
+                                        world=world, rank=rank, splits=args.splits or None, exchange=args.exchange)
+        else:
+            sh = sharding.HeadShardedDecode(qd, Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens,
+                                            world=world, rank=rank, splits=args.splits or None)
         del Kd, Vd
         torch.cuda.empty_cache()
         cache, ws, splits = sh.cache, sh.ws, sh.ws.splits
@@ -331,10 +337,19 @@ def main():
         def api_step():
             sh.step()
 
-        parallelism = (f"split-KV over {world} GPUs: NCCL all-gather of (out, lse) + merge_states kernel"
-                       if w.shard == "splitkv" else f"KV heads over {world} GPUs ({w.Hkv // world} each), no exchange")
+        if w.shard == "splitkv":
+            parallelism = {
+                "fused": f"split-KV over {world} GPUs: split merge stores (out, lse) slices into every GPU over "
+                         "NVLink and combines them (one decode + one merge launch)",
+                "nvlink": f"split-KV over {world} GPUs: (out, lse) states pushed to peers over NVLink "
+                          "(push_state + wait_merge_states kernels)",
+                "nccl": f"split-KV over {world} GPUs: NCCL all-gather of (out, lse) + merge_states kernel",
+            }[args.exchange]
+        else:
+            parallelism = f"KV heads over {world} GPUs ({w.Hkv // world} each), no exchange"
         scaling = "strong"
-        launches_per_step = (1 if splits <= 1 or ws.split_sem is not None else 2) + (1 if w.shard == "splitkv" else 0)
+        launches_per_step = (1 if splits <= 1 or "merge=in-kernel" in api.describe(qd, cache, ws) else 2) + (
+            {"fused": 0, "nvlink": 2, "nccl": 1}[args.exchange] if w.shard == "splitkv" else 0)
     else:
         qd, Kd, Vd, seq_lens = workloads.generate(w, dev, seed=w.seed + rank)
         cache = api.KVCache.from_logical(Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens)
@@ -361,9 +376,21 @@ def main():
 
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     flush = torch.empty(max(96 << 20, 3 * l2), dtype=torch.uint8, device=dev)
+    align_buf = torch.zeros(1, device=dev)
+
+    def prepare(i):
+        """Untimed before every step: the L2 flush and, with several ranks, a
+        device-side all-reduce so that every rank starts the step together
+        (a cross-GPU step is as fast as its slowest rank; without this the
+        skew between the ranks' flushes would be timed)."""
+        flush.fill_(i & 0xFF)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(align_buf)
 
     for i in range(args.warmup):
-        flush.fill_(i & 0xFF)
+        prepare(i)
         launch()
     torch.cuda.synchronize()
 
@@ -373,7 +400,7 @@ def main():
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
-            flush.fill_(i & 0xFF)
+            prepare(i)
             ev[i][0].record(stream)
             launch()
             ev[i][1].record(stream)
@@ -391,12 +418,12 @@ def main():
         evg = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
         for i in range(args.warmup):
-            flush.fill_(i & 0xFF)
+            prepare(i)
             gather_launch()
         torch.cuda.synchronize()
         barrier(world)
         for i in range(args.steps):
-            flush.fill_(i & 0xFF)
+            prepare(i)
             evg[i][0].record(stream)
             gather_launch()
             evg[i][1].record(stream)
@@ -409,14 +436,14 @@ def main():
     out_host = torch.empty_like(out, device="cpu").pin_memory()
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for i in range(args.warmup):
-        flush.fill_(i & 0xFF)
+        prepare(i)
         qd.copy_(q_host, non_blocking=True)
         api_step()
         out_host.copy_(out, non_blocking=True)
     torch.cuda.synchronize()
     barrier(world)
     for i in range(args.steps):
-        flush.fill_(i & 0xFF)
+        prepare(i)
         ev2[i][0].record(stream)
         qd.copy_(q_host, non_blocking=True)
         api_step()
@@ -445,6 +472,8 @@ def main():
             "config": w.config() | {"splits": splits, "payload_bytes_per_gpu": payload,
                                     "payload_bytes_total": total_payload,
                                     "l2": "flushed before every step (3 x L2 write)",
+                                    "rank_alignment": ("device-side all-reduce before every step, untimed"
+                                                       if world > 1 else None),
                                     "parallelism": parallelism},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": traffic,
@@ -464,6 +493,8 @@ def main():
         if world == 1 and args.cpu_sample_s > 0:
             line["cpu_baseline"] = cpu_baseline(w, args.cpu_sample_s)
         print(json.dumps(line), flush=True)
+    if sharded and w.shard == "splitkv":
+        sh.close()
     if world > 1:
         import torch.distributed as dist
 

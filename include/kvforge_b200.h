@@ -120,6 +120,67 @@ cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream);
 cudaError_t kvf_b200_merge_states(const float *o, const float *lse, int P, int rows, int d, long long o_stride,
                                   long long lse_stride, float *out, float *lse_out, cudaStream_t stream);
 
+/* Split-KV across GPUs, fused into the decode's split merge: each rank
+ * decodes its own token range, and the merge kernel that combines its splits
+ * also stores the result (normalised output and lse of every query head, in
+ * 32-column slices) straight into the gather buffer of every rank over NVLink,
+ * counts itself in on each rank with a system-scope atomic, waits (bounded)
+ * until all P ranks have arrived for its slice and writes the combination of
+ * the P parts (the same arithmetic as kvf_b200_merge_states) to out. One
+ * decode launch plus one merge launch per step, no collective library.
+ *   gather     this rank's buffer, [2][P][B*H][D+1] floats (two buffers
+ *              alternate by epoch parity; a rank runs at most one step ahead)
+ *   count      this rank's counters, [B*H][D/32] uint32, zero initially
+ *   peer_*     the same two buffers of rank p, mapped on this GPU (p = rank
+ *              included); epoch: 1, 2, 3, ... one per step. */
+typedef struct kvf_exchange {
+  int P, rank, epoch;
+  unsigned timeout_ms;
+  float *gather;
+  unsigned *count;
+  float *peer_gather[8];
+  unsigned *peer_count[8];
+} kvf_exchange;
+
+/* kvf_b200_decode over this rank's tokens with the cross-GPU combination
+ * fused into the split merge (a->splits must be > 1; split_sem is ignored).
+ * A wait that runs out of time zeroes its slice and sets bit 2 of
+ * kvf_b200_device_errors(). */
+cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                                     const kvf_exchange *x, cudaStream_t stream);
+
+/* Cross-GPU exchange of split-KV states over NVLink peer memory, without a
+ * collective library (no reference counterpart). A rank's packed state
+ * (`floats` floats: output then lse) is stored into its slot of each of the P
+ * ranks' gather buffers (peer_slots[p], device pointers valid on this GPU,
+ * e.g. from a symmetric allocation), followed by a system-scope fence and
+ * `epoch` written to peer_flags[p] (this rank's flag word on rank p). One
+ * block; at most 8 ranks. */
+cudaError_t kvf_b200_push_state(const float *state, int floats, float *const *peer_slots, int *const *peer_flags,
+                                int P, int epoch, cudaStream_t stream);
+
+/* Waits until flags[0..P) all hold `epoch` or later (bounded by timeout_ms;
+ * on timeout the rows are zeroed and kvf_b200_exchange_errors() reports it),
+ * then combines the P gathered states (part p at gathered + p * part_stride:
+ * output [rows][d], lse at + lse_off) like kvf_b200_merge_states. */
+cudaError_t kvf_b200_wait_merge_states(const float *gathered, const int *flags, int P, int epoch, int rows, int d,
+                                       long long part_stride, long long lse_off, float *out, float *lse_out,
+                                       unsigned timeout_ms, cudaStream_t stream);
+
+/* Nonzero if a wait of kvf_b200_wait_merge_states ran out of time since the
+ * last call (then cleared). */
+unsigned kvf_b200_exchange_errors(void);
+
+/* Zeroed device buffer shareable with other processes of the node:
+ * *ptr receives the device pointer, handle64 the 64-byte CUDA IPC handle. */
+cudaError_t kvf_b200_ipc_alloc(size_t bytes, void **ptr, void *handle64);
+/* Maps another process's buffer (peer access enabled); release with
+ * kvf_b200_ipc_close. */
+cudaError_t kvf_b200_ipc_open(const void *handle64, void **ptr);
+cudaError_t kvf_b200_ipc_close(void *ptr);
+/* Frees a buffer from kvf_b200_ipc_alloc. */
+cudaError_t kvf_b200_ipc_free(void *ptr);
+
 /* Launch by variant id, e.g. "int8_tm_p_g4_u2_d128": the registry lookup plus
  * call of bench/sweep.cu:180-184 (id format of src/codegen.cpp:59-65,
  * fmt_{hm,tm}_{c,p}_g{1,2,4,8}_u{2,4}_d{64,128}). Unknown ids return
@@ -147,8 +208,9 @@ cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int pa
 
 /* Device-side error word of the current device, then cleared. Bit 0: a
  * shared-memory barrier wait in a decode kernel ran out of time (the kernel
- * abandoned the step and its output is not valid). 0 = no error. This call
- * synchronises with the device. */
+ * abandoned the step and its output is not valid). Bit 1: a cross-GPU wait
+ * of kvf_b200_decode_exchange ran out of time (the affected output slices are
+ * zero). 0 = no error. This call synchronises with the device. */
 unsigned kvf_b200_device_errors(void);
 
 /* Quantizes `rows` logical rows of d fp32 channels (device memory) into the

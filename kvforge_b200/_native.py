@@ -74,6 +74,16 @@ SIGNATURES = [
     ("kvf_b200_merge", c_int, [ctypes.POINTER(KvfArgs), c_int, c_void_p]),
     ("kvf_b200_merge_states", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_longlong,
                                        ctypes.c_longlong, c_void_p, c_void_p, c_void_p]),
+    ("kvf_b200_decode_exchange", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                         c_void_p]),
+    ("kvf_b200_push_state", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    ("kvf_b200_wait_merge_states", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, ctypes.c_longlong,
+                                            ctypes.c_longlong, c_void_p, c_void_p, c_uint, c_void_p]),
+    ("kvf_b200_exchange_errors", c_uint, []),
+    ("kvf_b200_ipc_alloc", c_int, [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
+    ("kvf_b200_ipc_open", c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    ("kvf_b200_ipc_close", c_int, [c_void_p]),
+    ("kvf_b200_ipc_free", c_int, [c_void_p]),
     ("kvf_b200_decode_noalloc", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_launch_variant", c_int, [c_char_p, ctypes.POINTER(KvfArgs), c_void_p]),
     ("kvf_b200_variant_count", c_int, []),

@@ -27,7 +27,7 @@ OBJ = PKG / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}"]
-LIB_SOURCES = ["decode.cu", "registry.cu", "quantize.cu"]
+LIB_SOURCES = ["decode.cu", "registry.cu", "quantize.cu", "exchange.cu"]
 
 
 def nvcc() -> str:

@@ -282,7 +282,7 @@ cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int 
   return cudaSuccess;
 }
 
-cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl) {
+cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl, const kvf_exchange *x = nullptr) {
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)a->H, (unsigned)a->B, (unsigned)((d + 31) / 32));
@@ -295,6 +295,10 @@ cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   const kvf_args args = *a;
+  if (x) {
+    const kvf_exchange xc = *x;
+    return cudaLaunchKernelEx(&cfg, merge_exchange_kernel, args, d, xc);
+  }
   return cudaLaunchKernelEx(&cfg, merge_kernel, args, d);
 }
 
@@ -402,10 +406,11 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
   return cudaSuccess;
 }
 
-cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream) {
+cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, const kvf_exchange *x = nullptr) {
   TcLaunch L;
   cudaError_t e = plan_tc(a, sh, L);
   if (e != cudaSuccess) return e;
+  if (x) L.p.merge_in_kernel = 0;  // the exchange runs in the separate merge
   CUtensorMap tk, tv;
   e = encode_maps_box(a, sh, 128, 128, L.p.tbox, 1, tk, tv);
   if (e != cudaSuccess) return e;
@@ -416,7 +421,7 @@ cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream) {
   void *params[4] = {const_cast<kvf_args *>(&args), const_cast<TcPlan *>(&plan), &tk, &tv};
   e = cudaLaunchKernel(L.fn, dim3((unsigned)L.blocks), dim3((unsigned)kTcThreads), params, L.p.smem_total, stream);
   if (e != cudaSuccess) return e;
-  if (!L.p.final_out && !L.p.merge_in_kernel) e = launch_merge(a, sh.d, stream, true);
+  if (!L.p.final_out && !L.p.merge_in_kernel) e = launch_merge(a, sh.d, stream, true, x);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -425,13 +430,16 @@ cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream) {
 
 using namespace kvfb;
 
-extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
-                                       cudaStream_t stream) {
+namespace kvfb {
+namespace {
+
+cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int paged, cudaStream_t stream,
+                        const kvf_exchange *x) {
   Shape sh;
   cudaError_t e = check_args(a, fmt, d, g, ord, paged, sh);
   if (e != cudaSuccess) return e;
   if (a->B == 0) return cudaSuccess;
-  if (tc_applies(sh, a->B * a->Hkv)) return launch_tc(a, sh, stream);
+  if (tc_applies(sh, a->B * a->Hkv)) return launch_tc(a, sh, stream, x);
   Launch L;
   e = plan_launch(a, sh, L);
   if (e != cudaSuccess) return e;
@@ -446,8 +454,26 @@ extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g,
   e = cudaLaunchKernel(L.fn, dim3((unsigned)L.blocks), dim3((unsigned)L.threads), params,
                        L.p.smem_total, stream);
   if (e != cudaSuccess) return e;
-  if (!L.p.final_out) e = launch_merge(a, d, stream, true);
+  if (!L.p.final_out) e = launch_merge(a, d, stream, true, x);
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+} // namespace
+} // namespace kvfb
+
+extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                                       cudaStream_t stream) {
+  return decode_impl(a, fmt, d, g, ord, paged, stream, nullptr);
+}
+
+extern "C" cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                                                const kvf_exchange *x, cudaStream_t stream) {
+  if (!a || !x || a->splits <= 1 || x->P < 1 || x->P > 8 || x->rank < 0 || x->rank >= x->P || !x->gather ||
+      !x->count || x->timeout_ms == 0)
+    return cudaErrorInvalidValue;
+  for (int p = 0; p < x->P; ++p)
+    if (!x->peer_gather[p] || !x->peer_count[p]) return cudaErrorInvalidValue;
+  return decode_impl(a, fmt, d, g, ord, paged, stream, x);
 }
 
 extern "C" cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream) {

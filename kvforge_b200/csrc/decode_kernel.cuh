@@ -85,7 +85,7 @@ struct Plan {
 };
 
 __device__ unsigned g_kvfb_error;
-enum : unsigned { KVFB_ERR_TIMEOUT = 1u };
+enum : unsigned { KVFB_ERR_TIMEOUT = 1u, KVFB_ERR_EXCHANGE = 2u };
 
 // (scale, zero) of an fp16 half2 metadata word.
 __device__ __forceinline__ float2 meta_sz(uint32_t w) { return ptx::unpack_f16x2(w); }
@@ -869,14 +869,16 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
 constexpr int kMergeWarps = 8;
 constexpr int kMergeUnroll = 32;
 
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args a, int d) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float s_m[kMergeWarps], s_l[kMergeWarps];
-  __shared__ float s_o[kMergeWarps][32];
-  const long long head = (long long)blockIdx.y * a.H + blockIdx.x;
+// Merged (M, L, O) of one (query head, 32-column slice) over all splits, for
+// warp 0 (lane = column); the caller's block has kMergeWarps warps.
+struct MergeSmem {
+  float m[kMergeWarps], l[kMergeWarps];
+  float o[kMergeWarps][32];
+};
+
+__device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long head, int col, bool colok,
+                                             MergeSmem &sm, float &Mt, float &Lt, float &Ot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int col = blockIdx.z * 32 + lane;
-  const bool colok = col < d;
   const int S = a.splits;
   const float *ml = a.part_ml + head * S * 2;
   const float *po = a.part_o + head * (long long)S * d;
@@ -908,27 +910,109 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args 
     M = mx;
   }
   if (lane == 0) {
-    s_m[warp] = M;
-    s_l[warp] = L;
+    sm.m[warp] = M;
+    sm.l[warp] = L;
   }
-  s_o[warp][lane] = O;
+  sm.o[warp][lane] = O;
   __syncthreads();
+  Mt = -INFINITY;
+  Lt = 0.f;
+  Ot = 0.f;
   if (warp == 0) {
-    float Mt = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, s_m[w]);
-    float Lt = 0.f, Ot = 0.f;
+    for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, sm.m[w]);
     if (Mt != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kMergeWarps; ++w) {
-        const float wt = s_m[w] == -INFINITY ? 0.f : exp2f(s_m[w] - Mt);
-        Lt = fmaf(s_l[w], wt, Lt);
-        Ot = fmaf(s_o[w][lane], wt, Ot);
+        const float wt = sm.m[w] == -INFINITY ? 0.f : exp2f(sm.m[w] - Mt);
+        Lt = fmaf(sm.l[w], wt, Lt);
+        Ot = fmaf(sm.o[w][lane], wt, Ot);
       }
     }
+  }
+}
+
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args a, int d) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ MergeSmem sm;
+  const long long head = (long long)blockIdx.y * a.H + blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int col = blockIdx.z * 32 + lane;
+  const bool colok = col < d;
+  float Mt, Lt, Ot;
+  merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot);
+  if ((threadIdx.x >> 5) == 0) {
     if (colok) a.out[head * d + col] = Lt > 0.f ? Ot / Lt : 0.f;
     if (lane == 0 && blockIdx.z == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
   }
+}
+
+// The split merge of one rank of a split-KV decode across GPUs, fused with
+// the cross-GPU exchange (see kvf_b200_decode_exchange): this rank's
+// (output slice, lse) goes into every rank's gather buffer, each rank's
+// counter for the slice is raised, and once all P parts of the slice are
+// present (bounded wait) they are combined into out.
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_exchange_kernel(const kvf_args a, int d,
+                                                                         const kvf_exchange x) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ MergeSmem sm;
+  const long long head = (long long)blockIdx.y * a.H + blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int col = blockIdx.z * 32 + lane;
+  const bool colok = col < d;
+  float Mt, Lt, Ot;
+  merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot);
+  if ((threadIdx.x >> 5) != 0) return;
+  const long long rows = (long long)a.B * a.H;
+  const int nz = gridDim.z;
+  const long long stride = d + 1;                 // floats per (rank, row): output then lse
+  const long long par = (long long)(x.epoch & 1) * x.P;
+  const float val = Lt > 0.f ? Ot / Lt : 0.f;
+  const float lse = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
+  const unsigned slot = (unsigned)(head * nz + blockIdx.z);
+  for (int p = 0; p < x.P; ++p) {
+    float *g = x.peer_gather[p] + ((par + x.rank) * rows + head) * stride;
+    if (colok) g[col] = val;
+    if (lane == 0) g[d] = lse;
+  }
+  __threadfence_system();
+  __syncwarp();
+  __shared__ int s_ok;
+  if (lane == 0) {
+    for (int p = 0; p < x.P; ++p) atomicAdd_system(x.peer_count[p] + slot, 1u);
+    // All P parts of this slice are present once the counter reaches P * epoch.
+    const unsigned want = (unsigned)x.P * (unsigned)x.epoch;
+    const uint64_t t0 = ptx::globaltimer_ns();
+    const uint64_t limit = (uint64_t)x.timeout_ms * 1000000ull;
+    int ok = 1;
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(x.count + slot) : "memory");
+      if ((int)(v - want) >= 0) break;
+      if (ptx::globaltimer_ns() - t0 > limit) {
+        ok = 0;
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (!ok) atomicOr(&g_kvfb_error, KVFB_ERR_EXCHANGE);
+    s_ok = ok;
+  }
+  __syncwarp();
+  float M = -INFINITY;
+  const float *base = x.gather + par * rows * stride + head * stride;
+  for (int p = 0; p < x.P; ++p) M = fmaxf(M, __ldcg(base + p * rows * stride + d));
+  float W = 0.f, O = 0.f;
+  if (M != -INFINITY && s_ok) {
+    for (int p = 0; p < x.P; ++p) {
+      const float lp = __ldcg(base + p * rows * stride + d);
+      const float w = lp == -INFINITY ? 0.f : exp2f(lp - M);
+      W += w;
+      if (colok && w > 0.f) O = fmaf(w, __ldcg(base + p * rows * stride + col), O);
+    }
+  }
+  if (colok) a.out[head * d + col] = W > 0.f ? O / W : 0.f;
+  if (lane == 0 && blockIdx.z == 0 && a.lse) a.lse[head] = W > 0.f ? M + log2f(W) : -INFINITY;
 }
 
 // Combination of attention states over disjoint token ranges (no reference

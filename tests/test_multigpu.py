@@ -3,9 +3,11 @@
 * kvf_b200_merge_states: decoding disjoint token ranges separately (with the
   lse output) and combining them equals one decode over all tokens, and the
   oracle, on one GPU;
-* with two or more GPUs, two NCCL ranks run the split-KV and the KV-head
-  protocols end to end and must match a single-GPU decode of the same
-  inputs (skipped on a one-GPU box).
+* with two or more GPUs, two ranks run the split-KV protocol (exchange fused
+  into the split merge, separate NVLink push/merge kernels, NCCL all-gather;
+  several steps each) and the KV-head protocol end
+  to end and must match a single-GPU decode of the same inputs (skipped on a
+  one-GPU box).
 """
 from __future__ import annotations
 
@@ -21,6 +23,7 @@ from oracle import oracle as O
 torch = pytest.importorskip("torch")
 
 from kvforge_b200 import FMT_F16, FMT_INT4, FMT_INT8, ORD_HEAD, ORD_TOKEN, api, sharding  # noqa: E402
+from kvforge_b200._native import lib  # noqa: E402
 from kvforge_b200.layout import Placement  # noqa: E402
 
 pytestmark = pytest.mark.gpu
@@ -89,15 +92,19 @@ def _rank(rank, world, port, results):
     try:
         q, K, V = _inputs(dev, "splitkv")
         lens = np.array([4321], dtype=np.int32)
-        sk = sharding.SplitKVDecode(q, K, V, fmt=FMT_INT4, group=32, place=Placement(ORD_HEAD, False, 0),
-                                    seq_lens=lens, world=world, rank=rank)
-        a = sk.step().cpu().numpy()
+        a = {}
+        for exchange in ("fused", "nvlink", "nccl"):
+            sk = sharding.SplitKVDecode(q, K, V, fmt=FMT_INT4, group=32, place=Placement(ORD_HEAD, False, 0),
+                                        seq_lens=lens, world=world, rank=rank, exchange=exchange)
+            for _ in range(3):  # several steps: epochs and the two gather buffers alternate
+                a[exchange] = sk.step().cpu().numpy()
+            sk.close()
         q, K, V = _inputs(dev, "kvheads")
         hs = sharding.HeadShardedDecode(q, K, V, fmt=FMT_INT8, group=64, place=Placement(ORD_TOKEN, True, 16),
                                         seq_lens=None, world=world, rank=rank)
         b = hs.step(gather=True).cpu().numpy()
         torch.cuda.synchronize()
-        results[rank] = (a, b, api.device_errors())
+        results[rank] = (a, b, api.device_errors() | lib().kvf_b200_exchange_errors())
     finally:
         dist.destroy_process_group()
 
@@ -121,5 +128,6 @@ def test_two_nccl_ranks_match_one_gpu():
     for r in range(world):
         a, b, errs = res[r]
         assert errs == 0
-        assert np.abs(a - ref_a).max() < 1e-5, r
+        for exchange, got in a.items():
+            assert np.abs(got - ref_a).max() < 1e-5, (r, exchange)
         assert np.abs(b - ref_b).max() < 1e-6, r
