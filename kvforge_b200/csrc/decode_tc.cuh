@@ -335,8 +335,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         bool progress = false;
         if (ns < ntiles) {
           const int s = ns % p.stages, j = ns & 1;
-          if (ptx::mbar_try_wait(bar_full + 8u * s, (uint32_t)((ns / p.stages) & 1)) &&
-              (ns < 2 || ptx::mbar_try_wait(bar_sfree + 8u * j, (uint32_t)(((ns >> 1) - 1) & 1)))) {
+          if (ptx::mbar_test_wait(bar_full + 8u * s, (uint32_t)((ns / p.stages) & 1)) &&
+              (ns < 2 || ptx::mbar_test_wait(bar_sfree + 8u * j, (uint32_t)(((ns >> 1) - 1) & 1)))) {
             tc::fence_after();
             const uint32_t sk = sbase + (uint32_t)s * p.stage_bytes;
 #pragma unroll
@@ -353,7 +353,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
             progress = true;
           }
         }
-        if (npv < ns && ptx::mbar_try_wait(bar_pready, (uint32_t)(npv & 1))) {
+        if (npv < ns && ptx::mbar_test_wait(bar_pready, (uint32_t)(npv & 1))) {
           tc::fence_after();
           const uint32_t sv = sbase + (uint32_t)(npv % p.stages) * p.stage_bytes + TB * 128u;
 #pragma unroll

@@ -57,6 +57,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase: never suspends the thread, for loops that
+// poll several barriers in turn (try_wait may suspend until a hardware time
+// limit while another barrier is already complete).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for phase `parity` of the barrier to complete. Gives up after
 // `limit_ns` of wall-clock time and returns false; the caller records the
 // error and unwinds.
