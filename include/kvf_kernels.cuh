@@ -68,4 +68,18 @@ cudaError_t launch(const Args &a, cudaStream_t st) {
   return kvf_b200_decode(c_args(a), FMT, D, G, ORD, PAGED ? 1 : 0, st);
 }
 
+// launch<> pinned to one sm_100a kernel path (KVF_PATH_MMA or KVF_PATH_TC),
+// the extra template parameter the sm_100a dispatch tables
+// (kvforge_b200/codegen.py) instantiate for "_mma" / "_tc" variant ids.
+template <int FMT, int D, int G, int U, int ORD, bool PAGED, int PATH>
+cudaError_t launch_path(const Args &a, cudaStream_t st) {
+  static_assert(FMT == FMT_F16 || FMT == FMT_INT8 || FMT == FMT_INT4, "format");
+  static_assert(D == 64 || D == 128, "head dimension");
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "GQA pack size");
+  static_assert(U == 2 || U == 4, "unroll");
+  static_assert(PATH == KVF_PATH_AUTO || PATH == KVF_PATH_MMA || PATH == KVF_PATH_TC, "kernel path");
+  static_assert(PATH != KVF_PATH_TC || (FMT == FMT_INT8 && D == 128), "the tcgen05 kernel takes int8 rows of 128");
+  return kvf_b200_decode_path(c_args(a), FMT, D, G, ORD, PAGED ? 1 : 0, PATH, st);
+}
+
 } // namespace kvf

@@ -103,6 +103,22 @@ typedef struct kvf_args {
 cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
                             cudaStream_t stream);
 
+/* Kernel paths of the sm_100a decode (the B200 counterpart of the plan's
+ * "mma on/off" choice):
+ *   KVF_PATH_AUTO  by shape: the tcgen05 kernel for int8 rows of 128
+ *                  dimensions with one or two quantization groups once there
+ *                  are >= 64 (sequence, KV head) units, else mma.sync; the
+ *                  environment variable KVF_B200_TC=1/0 forces one of them;
+ *   KVF_PATH_MMA   always the mma.sync kernel (every format);
+ *   KVF_PATH_TC    always the tcgen05 kernel; shapes it does not cover return
+ *                  cudaErrorNotSupported without launching. */
+enum { KVF_PATH_AUTO = 0, KVF_PATH_MMA = 1, KVF_PATH_TC = 2 };
+
+/* kvf_b200_decode on an explicit kernel path (KVF_PATH_*); any other path
+ * value returns cudaErrorInvalidValue. kvf_b200_decode is path AUTO. */
+cudaError_t kvf_b200_decode_path(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path,
+                                 cudaStream_t stream);
+
 /* The split merge alone (decode_merge<D>, runtime/kvf_kernels.cuh:288-306):
  * out[b][h] = sum_s part_o[s] * 2^(m_s - M) / sum_s l_s * 2^(m_s - M). */
 cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream);
@@ -188,8 +204,13 @@ cudaError_t kvf_b200_ipc_free(void *ptr);
 cudaError_t kvf_b200_launch_variant(const char *variant_id, const kvf_args *a,
                                     cudaStream_t stream);
 
-/* Number of variant ids this library registers, and the i-th id (NULL when i
- * is out of range). Mirrors kvf_register_all (gen/kvf_dispatch.cu). */
+/* Variant ids may end in "_mma" or "_tc" to pin the kernel path
+ * (KVF_PATH_MMA / KVF_PATH_TC); without a suffix the path is AUTO. "_tc" ids
+ * exist for int8 rows of 128 dimensions only.
+ *
+ * Number of variant ids this library registers, and the i-th id (NULL when i
+ * is out of range). Mirrors kvf_register_all (gen/kvf_dispatch.cu, and the
+ * sm_100a tables kvforge_b200/codegen.py emits). */
 int kvf_b200_variant_count(void);
 const char *kvf_b200_variant_name(int i);
 
@@ -205,6 +226,9 @@ int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int gr
  * launching anything. */
 cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged, char *buf,
                               int buf_len);
+/* kvf_b200_describe for an explicit kernel path (KVF_PATH_*). */
+cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d, int ord, int paged, int path, char *buf,
+                                   int buf_len);
 
 /* Device-side error word of the current device, then cleared. Bit 0: a
  * shared-memory barrier wait in a decode kernel ran out of time (the kernel

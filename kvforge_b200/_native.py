@@ -71,6 +71,7 @@ _lib = None
 # (name, restype, argtypes) of every exported entry point.
 SIGNATURES = [
     ("kvf_b200_decode", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    ("kvf_b200_decode_path", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_merge", c_int, [ctypes.POINTER(KvfArgs), c_int, c_void_p]),
     ("kvf_b200_merge_states", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_longlong,
                                        ctypes.c_longlong, c_void_p, c_void_p, c_void_p]),
@@ -90,6 +91,7 @@ SIGNATURES = [
     ("kvf_b200_variant_name", c_char_p, [c_int]),
     ("kvf_b200_suggest_splits", c_int, [c_int] * 9),
     ("kvf_b200_describe", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_char_p, c_int]),
+    ("kvf_b200_describe_path", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_char_p, c_int]),
     ("kvf_b200_device_errors", c_uint, []),
     ("kvf_b200_quantize", c_int, [c_int, c_int, c_int, c_void_p, c_longlong, c_void_p, c_void_p, c_void_p]),
     ("kvf_b200_version", c_char_p, []),

@@ -190,15 +190,25 @@ def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace)
     return a
 
 
+PATHS = {"auto": 0, "mma": 1, "tc": 2}  # KVF_PATH_AUTO / KVF_PATH_MMA / KVF_PATH_TC
+
+
+def _path(path: str) -> int:
+    if path not in PATHS:
+        raise ValueError(f"path must be one of {sorted(PATHS)}")
+    return PATHS[path]
+
+
 def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = None,
            splits: Optional[int] = None, workspace: Optional[Workspace] = None, stream=None,
-           g: int = 1, lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+           g: int = 1, lse: Optional[torch.Tensor] = None, path: str = "auto") -> torch.Tensor:
     """One decode step: out[b][h] = softmax(q k^T * scale) v over the cache.
 
     q: float32 [B][H][D] on the cache's device. Returns out (float32 [B][H][D]).
     lse (optional float32 [B][H]) receives log2 of each head's softmax
     denominator, for combining outputs over disjoint token ranges with
-    merge_states."""
+    merge_states. path: "auto" (the launcher chooses), "mma" (mma.sync
+    kernel) or "tc" (tcgen05 kernel; int8 rows of 128 only)."""
     if q.dtype != torch.float32 or not q.is_contiguous():
         raise ValueError("q must be a contiguous float32 tensor [B][H][D]")
     B, H, d = q.shape
@@ -213,9 +223,9 @@ def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = Non
             raise ValueError("lse must be a contiguous float32 tensor [B][H]")
         a.lse = lse.data_ptr()
     check(
-        "kvf_b200_decode",
-        lib().kvf_b200_decode(ctypes.byref(a), cache.fmt, d, g, cache.place.order,
-                              int(cache.place.paged), _stream(stream)),
+        "kvf_b200_decode_path",
+        lib().kvf_b200_decode_path(ctypes.byref(a), cache.fmt, d, g, cache.place.order,
+                                   int(cache.place.paged), _path(path), _stream(stream)),
     )
     return out
 
@@ -241,15 +251,15 @@ def merge_states(outs: torch.Tensor, lses: torch.Tensor, out: Optional[torch.Ten
     return out
 
 
-def describe(q: torch.Tensor, cache: KVCache, workspace: Workspace) -> str:
-    out = torch.empty(0)
+def describe(q: torch.Tensor, cache: KVCache, workspace: Workspace, path: str = "auto") -> str:
+    """One line describing the launch decode() would make (kernel, grid,
+    stages, shared memory, splits), without launching."""
     B, H, d = q.shape
     a = make_args(q, cache, q, workspace)
     buf = ctypes.create_string_buffer(512)
-    check("kvf_b200_describe",
-          lib().kvf_b200_describe(ctypes.byref(a), cache.fmt, d, cache.place.order,
-                                  int(cache.place.paged), buf, 512))
-    del out
+    check("kvf_b200_describe_path",
+          lib().kvf_b200_describe_path(ctypes.byref(a), cache.fmt, d, cache.place.order,
+                                       int(cache.place.paged), _path(path), buf, 512))
     return buf.value.decode()
 
 
@@ -257,5 +267,5 @@ def device_errors() -> int:
     return int(lib().kvf_b200_device_errors())
 
 
-__all__ = ["KVCache", "Workspace", "decode", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
+__all__ = ["KVCache", "Workspace", "decode", "PATHS", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
            "device_errors", "row_bytes", "groups_per_row", "scale_log2", "FMT_F16", "FMT_INT8", "FMT_INT4"]

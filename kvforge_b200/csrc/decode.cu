@@ -337,11 +337,33 @@ uint32_t tc_misc_bytes(int gpr, int nh) {
 // KVF_B200_TC=1 forces it for every shape it supports, KVF_B200_TC=0 never.
 constexpr int kTcMinUnits = 64;
 
+bool tc_supported(const Shape &sh) { return sh.fmt == 1 && sh.d == 128 && (sh.gpr == 1 || sh.gpr == 2); }
+
 bool tc_applies(const Shape &sh, int units) {
   const char *e = std::getenv("KVF_B200_TC");
   const bool forced = e && e[0] == '1';
-  if (!tc_enabled() || sh.fmt != 1 || sh.d != 128 || (sh.gpr != 1 && sh.gpr != 2)) return false;
+  if (!tc_enabled() || !tc_supported(sh)) return false;
   return forced || units >= kTcMinUnits;
+}
+
+// The kernel a launch on `path` runs: 1 = mma.sync, 2 = tcgen05; an error
+// status for a path value that does not exist or a tcgen05 request the shape
+// does not allow.
+cudaError_t resolve_path(const Shape &sh, int units, int path, int &kernel) {
+  switch (path) {
+  case KVF_PATH_AUTO:
+    kernel = tc_applies(sh, units) ? 2 : 1;
+    return cudaSuccess;
+  case KVF_PATH_MMA:
+    kernel = 1;
+    return cudaSuccess;
+  case KVF_PATH_TC:
+    if (!tc_supported(sh)) return cudaErrorNotSupported;
+    kernel = 2;
+    return cudaSuccess;
+  default:
+    return cudaErrorInvalidValue;
+  }
 }
 
 struct TcLaunch {
@@ -433,13 +455,16 @@ using namespace kvfb;
 namespace kvfb {
 namespace {
 
-cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int paged, cudaStream_t stream,
+cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path, cudaStream_t stream,
                         const kvf_exchange *x) {
   Shape sh;
   cudaError_t e = check_args(a, fmt, d, g, ord, paged, sh);
   if (e != cudaSuccess) return e;
+  int kernel = 1;
+  e = resolve_path(sh, a->B * a->Hkv, path, kernel);
+  if (e != cudaSuccess) return e;
   if (a->B == 0) return cudaSuccess;
-  if (tc_applies(sh, a->B * a->Hkv)) return launch_tc(a, sh, stream, x);
+  if (kernel == 2) return launch_tc(a, sh, stream, x);
   Launch L;
   e = plan_launch(a, sh, L);
   if (e != cudaSuccess) return e;
@@ -463,7 +488,12 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
 
 extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
                                        cudaStream_t stream) {
-  return decode_impl(a, fmt, d, g, ord, paged, stream, nullptr);
+  return decode_impl(a, fmt, d, g, ord, paged, KVF_PATH_AUTO, stream, nullptr);
+}
+
+extern "C" cudaError_t kvf_b200_decode_path(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path,
+                                            cudaStream_t stream) {
+  return decode_impl(a, fmt, d, g, ord, paged, path, stream, nullptr);
 }
 
 extern "C" cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
@@ -473,7 +503,7 @@ extern "C" cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int 
     return cudaErrorInvalidValue;
   for (int p = 0; p < x->P; ++p)
     if (!x->peer_gather[p] || !x->peer_count[p]) return cudaErrorInvalidValue;
-  return decode_impl(a, fmt, d, g, ord, paged, stream, x);
+  return decode_impl(a, fmt, d, g, ord, paged, KVF_PATH_AUTO, stream, x);
 }
 
 extern "C" cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream) {
@@ -495,12 +525,15 @@ extern "C" cudaError_t kvf_b200_merge_states(const float *o, const float *lse, i
   return cudaGetLastError();
 }
 
-extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged,
-                                         char *buf, int buf_len) {
+extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d, int ord, int paged, int path,
+                                              char *buf, int buf_len) {
   Shape sh;
   cudaError_t e = check_args(a, fmt, d, 1, ord, paged, sh);
   if (e != cudaSuccess) return e;
-  if (tc_applies(sh, a->B * a->Hkv)) {
+  int kernel = 1;
+  e = resolve_path(sh, a->B * a->Hkv, path, kernel);
+  if (e != cudaSuccess) return e;
+  if (kernel == 2) {
     TcLaunch T;
     e = plan_tc(a, sh, T);
     if (e != cudaSuccess) return e;
@@ -527,6 +560,11 @@ extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int 
                   L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out);
   }
   return cudaSuccess;
+}
+
+extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged, char *buf,
+                                         int buf_len) {
+  return kvf_b200_describe_path(a, fmt, d, ord, paged, KVF_PATH_AUTO, buf, buf_len);
 }
 
 extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group,

@@ -43,9 +43,12 @@ def test_version_and_variants():
     l = lib()
     assert b"sm_100a" in l.kvf_b200_version()
     count = l.kvf_b200_variant_count()
-    assert count == 3 * 2 * 2 * 2 * 4 * 2
+    base = 3 * 2 * 2 * 2 * 4 * 2  # the reference's ids (src/codegen.cpp:119-172 over d 64/128, g 1/2/4/8)
+    assert count == base + base + 2 * 2 * 4 * 2  # + every id pinned to mma.sync + int8 d128 ids on tcgen05
     names = {l.kvf_b200_variant_name(i).decode() for i in range(count)}
     assert "int8_tm_p_g4_u2_d128" in names and "f16_hm_c_g1_u4_d64" in names
+    assert "f16_hm_c_g1_u4_d64_mma" in names and "int8_tm_p_g8_u2_d128_tc" in names
+    assert "int8_tm_p_g8_u2_d64_tc" not in names and "f16_hm_c_g1_u2_d128_tc" not in names
     assert l.kvf_b200_variant_name(count) is None
     assert l.kvf_b200_variant_name(-1) is None
 
@@ -53,7 +56,8 @@ def test_version_and_variants():
 def test_unknown_variant_rejected_without_launch():
     a = KvfArgs()
     for bad in [b"f32_hm_c_g1_u2_d128", b"int8_xx_c_g1_u2_d128", b"int8_hm_c_g3_u2_d128",
-                b"int8_hm_c_g1_u2_d96", b"int8_hm_c_g1_u2_d128x", b""]:
+                b"int8_hm_c_g1_u2_d96", b"int8_hm_c_g1_u2_d128x", b"", b"f16_hm_c_g1_u2_d128_tc",
+                b"int8_hm_c_g1_u2_d64_tc", b"int8_hm_c_g1_u2_d128_mmaa", b"int8_hm_c_g1_u2_d128_"]:
         assert lib().kvf_b200_launch_variant(bad, ctypes.byref(a), None) == 98  # InvalidDeviceFunction
 
 
@@ -138,3 +142,16 @@ def test_suggest_splits_without_gpu():
     assert 1 <= s5 <= 32
     assert l.kvf_b200_suggest_splits(1, 8, 8, 100, 0, 64, 0, 0, 0) >= 1
     assert l.kvf_b200_suggest_splits(0, 8, 8, 100, 0, 64, 0, 0, 0) == 1
+
+
+def test_kernel_path_errors_need_no_gpu():
+    """An explicit path is checked before anything launches: tcgen05 for a
+    format it does not take is cudaErrorNotSupported, an unknown path
+    cudaErrorInvalidValue (empty batch, so nothing would run either way)."""
+    a = KvfArgs()
+    a.B, a.H, a.Hkv, a.n, a.splits = 0, 32, 8, 16, 1
+    l = lib()
+    for path, want in [(0, 0), (1, 0), (2, 801), (3, 1), (-1, 1)]:
+        assert l.kvf_b200_decode_path(ctypes.byref(a), 0, 128, 1, 0, 0, path, None) == want, path
+    buf = ctypes.create_string_buffer(64)
+    assert l.kvf_b200_describe_path(ctypes.byref(a), 0, 128, 0, 0, 2, buf, 64) == 801

@@ -291,6 +291,42 @@ def test_forced_tcgen05_kernel_is_the_one_that_runs(cuda, monkeypatch):
     assert api.describe(q, cache, ws).startswith("kernel=mma.sync")
 
 
+@pytest.mark.parametrize("place", [Placement(ORD_TOKEN, False, 0), Placement(ORD_HEAD, True, 16)],
+                         ids=lambda p: p.name)
+def test_path_pinned_variants_run_their_kernel(cuda, monkeypatch, place):
+    """The "_tc" / "_mma" variant ids (and api.decode(path=...)) run the named
+    kernel whatever the launcher would choose, with the same results."""
+    monkeypatch.delenv("KVF_B200_TC", raising=False)
+    rs = np.random.RandomState(23)
+    B, H, Hkv, D, n = 2, 32, 8, 128, 700
+    q = rs.standard_normal((B, H, D)).astype(np.float32)
+    K = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
+    V = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
+    qd = torch.as_tensor(q, device=cuda)
+    cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                     fmt=FMT_INT8, group=64, place=place)
+    ws = api.Workspace.allocate(B, H, D, 3, cuda)
+    assert api.describe(qd, cache, ws, path="tc").startswith("kernel=tcgen05")
+    assert api.describe(qd, cache, ws, path="mma").startswith("kernel=mma.sync")
+    _, _, kd = O.quantize(FMT_INT8, D, 64, K.reshape(-1, D))
+    _, _, vd = O.quantize(FMT_INT8, D, 64, V.reshape(-1, D))
+    ref = O.attention(q, kd.reshape(K.shape), vd.reshape(V.shape), O.scale_f32(D))
+    base = f"int8_{'tm' if place.order == ORD_TOKEN else 'hm'}_{'p' if place.paged else 'c'}_g4_u2_d128"
+    outs = {}
+    for suffix in ("_tc", "_mma", ""):
+        outs[suffix] = run(q, K, V, FMT_INT8, 64, place, 3, variant=base + suffix)
+        assert_close(outs[suffix], ref, base + suffix)
+    for path in ("tc", "mma"):
+        got = api.decode(qd, cache, workspace=ws, path=path)
+        torch.cuda.synchronize()
+        assert_close(got.cpu().numpy(), ref, path)
+    assert api.device_errors() == 0
+    with pytest.raises(Exception):
+        f16 = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                       fmt=FMT_F16, group=0, place=place)
+        api.decode(qd, f16, workspace=ws, path="tc")
+
+
 def test_merge_entry_point_recombines_partials(cuda):
     rs = np.random.RandomState(14)
     B, H, Hkv, D, n = 1, 8, 8, 64, 1000
