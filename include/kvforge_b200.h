@@ -107,7 +107,7 @@ cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, i
  * "mma on/off" choice):
  *   KVF_PATH_AUTO  by shape: the tcgen05 kernel for int8 rows of 128
  *                  dimensions with one or two quantization groups once there
- *                  are >= 64 (sequence, KV head) units, else mma.sync; the
+ *                  are >= 32 (sequence, KV head) units, else mma.sync; the
  *                  environment variable KVF_B200_TC=1/0 forces one of them;
  *   KVF_PATH_MMA   always the mma.sync kernel (every format);
  *   KVF_PATH_TC    always the tcgen05 kernel; shapes it does not cover return

@@ -333,9 +333,11 @@ uint32_t tc_misc_bytes(int gpr, int nh) {
 }
 
 // The tensor-core kernel takes one KV head per block; it wins once there are
-// enough (sequence, KV head) units to fill the GPU without many splits.
+// enough (sequence, KV head) units to fill the GPU without many splits. The
+// B200 sweep (machines/b200-sxm.sweep.csv) puts the crossover between 8 units
+// (mma.sync 25.6 us vs 30.8 us) and 32 units (tcgen05 43.1 us vs 45.9 us).
 // KVF_B200_TC=1 forces it for every shape it supports, KVF_B200_TC=0 never.
-constexpr int kTcMinUnits = 64;
+constexpr int kTcMinUnits = 32;
 
 bool tc_supported(const Shape &sh) { return sh.fmt == 1 && sh.d == 128 && (sh.gpr == 1 || sh.gpr == 2); }
 
