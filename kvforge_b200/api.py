@@ -136,8 +136,8 @@ class KVCache:
 class Workspace:
     """Split partials: part_o [B][H][splits][D] and part_ml [B][H][splits][2].
 
-    ``split_sem`` (zeroed uint32 counters, two per (sequence, query head),
-    enough for any Hkv <= H) lets the tensor-core kernel merge the splits
+    ``split_sem`` (2 * B * H zeroed uint32 counters; the kernel uses two per
+    (sequence, KV head), so any Hkv <= H fits) lets the tensor-core kernel merge the splits
     itself: the last block of a (sequence, KV head) merges and resets the
     counters. ``fused=False`` leaves it out: a separate merge kernel, as in
     the reference.
