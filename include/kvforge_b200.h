@@ -119,6 +119,19 @@ enum { KVF_PATH_AUTO = 0, KVF_PATH_MMA = 1, KVF_PATH_TC = 2 };
 cudaError_t kvf_b200_decode_path(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path,
                                  cudaStream_t stream);
 
+/* One decode step whose queries come from host memory, with no copy-engine
+ * transfer: a small kernel reads q_host (B*H*d floats, 16-byte aligned, in
+ * pinned host memory the device addresses at the same pointer, e.g. from
+ * cudaHostAlloc) into a->q, and the decode (on `path`, KVF_PATH_*) is launched
+ * as its programmatic dependent, so the K/V stream starts while the queries
+ * are still in flight; the decode reads them only once the copy kernel has
+ * completed. a->out (and a->lse) may likewise point at such host memory: the
+ * kernels then write the result there directly. Host buffers the device cannot
+ * address (pageable memory) are rejected with cudaErrorInvalidValue before
+ * anything launches. Otherwise as kvf_b200_decode_path. */
+cudaError_t kvf_b200_decode_from_host(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path,
+                                      const float *q_host, cudaStream_t stream);
+
 /* The split merge alone (decode_merge<D>, runtime/kvf_kernels.cuh:288-306):
  * out[b][h] = sum_s part_o[s] * 2^(m_s - M) / sum_s l_s * 2^(m_s - M). */
 cudaError_t kvf_b200_merge(const kvf_args *a, int d, cudaStream_t stream);

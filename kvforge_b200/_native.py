@@ -72,6 +72,8 @@ _lib = None
 SIGNATURES = [
     ("kvf_b200_decode", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("kvf_b200_decode_path", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    ("kvf_b200_decode_from_host", c_int,
+     [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("kvf_b200_merge", c_int, [ctypes.POINTER(KvfArgs), c_int, c_void_p]),
     ("kvf_b200_merge_states", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_longlong,
                                        ctypes.c_longlong, c_void_p, c_void_p, c_void_p]),

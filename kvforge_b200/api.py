@@ -230,6 +230,84 @@ def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = Non
     return out
 
 
+class Decoder:
+    """Repeated decode steps of a fixed batch over one cache, as a CUDA graph.
+
+    One step takes the queries from a pinned host buffer (q_host), decodes
+    (kernel plus split merge) and leaves the output in a pinned host buffer
+    (out_host). The work is captured once and each step is a single graph
+    replay. With zero_copy (the default) there is no copy-engine transfer at
+    all: a small kernel reads the queries over PCIe while the decode kernel
+    already streams K/V (kvf_b200_decode_from_host), and the kernels write
+    the output straight into out_host; otherwise the step is an H2D copy, the
+    decode and a D2H copy.
+
+        dec = Decoder(cache, H)
+        out = dec.step(q)          # q: host float32 [B][H][D]; or
+        dec.q_host.copy_(q); dec.replay(); torch.cuda.current_stream().synchronize()
+
+    The cache, batch, split count and kernel path are fixed at construction;
+    the graph reads the cache in place, so its contents may change between
+    steps.
+    """
+
+    def __init__(self, cache: KVCache, H: int, *, splits: Optional[int] = None, path: str = "auto",
+                 g: int = 1, graph: bool = True, zero_copy: bool = True):
+        dev = cache.k.device
+        B, d = cache.B, cache.d
+        self.cache = cache
+        self.zero_copy = zero_copy
+        self.splits = splits if splits is not None else suggest_splits(cache, H)
+        self.q = torch.zeros((B, H, d), dtype=torch.float32, device=dev)
+        self.out = torch.zeros((B, H, d), dtype=torch.float32, device=dev)
+        self.q_host = torch.zeros((B, H, d), dtype=torch.float32).pin_memory()
+        self.out_host = torch.zeros((B, H, d), dtype=torch.float32).pin_memory()
+        self.workspace = Workspace.allocate(B, H, d, self.splits, dev)
+        self._args = make_args(self.q, cache, self.out, self.workspace)
+        if zero_copy:
+            self._args.out = self.out_host.data_ptr()
+        self._code = (cache.fmt, d, g, cache.place.order, int(cache.place.paged), _path(path))
+        self.graph = None
+        if graph:
+            # Warm up outside the capture (first launches set kernel attributes).
+            self._issue(torch.cuda.current_stream(dev))
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._issue(torch.cuda.current_stream(dev))
+            torch.cuda.synchronize(dev)
+
+    def _issue(self, stream) -> None:
+        fmt, d, g, order, paged, path = self._code
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        if self.zero_copy:
+            check("kvf_b200_decode_from_host",
+                  lib().kvf_b200_decode_from_host(ctypes.byref(self._args), fmt, d, g, order, paged, path,
+                                                  ctypes.c_void_p(self.q_host.data_ptr()), sp))
+            return
+        self.q.copy_(self.q_host, non_blocking=True)
+        check("kvf_b200_decode_path",
+              lib().kvf_b200_decode_path(ctypes.byref(self._args), fmt, d, g, order, paged, path, sp))
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def replay(self) -> None:
+        """One step on the current stream, asynchronously: out_host is valid
+        once the stream has reached this point."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._issue(torch.cuda.current_stream(self.q.device))
+
+    def step(self, q: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One step, synchronously: q (host float32 [B][H][D]) if given is
+        copied into q_host first; returns out_host."""
+        if q is not None:
+            self.q_host.copy_(q)
+        self.replay()
+        torch.cuda.current_stream(self.q.device).synchronize()
+        return self.out_host
+
+
 def merge_states(outs: torch.Tensor, lses: torch.Tensor, out: Optional[torch.Tensor] = None,
                  stream=None) -> torch.Tensor:
     """Combines P outputs of the same heads over disjoint token ranges:
@@ -267,5 +345,5 @@ def device_errors() -> int:
     return int(lib().kvf_b200_device_errors())
 
 
-__all__ = ["KVCache", "Workspace", "decode", "PATHS", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
+__all__ = ["KVCache", "Workspace", "Decoder", "decode", "PATHS", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
            "device_errors", "row_bytes", "groups_per_row", "scale_log2", "FMT_F16", "FMT_INT8", "FMT_INT4"]

@@ -430,7 +430,28 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
   return cudaSuccess;
 }
 
-cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, const kvf_exchange *x = nullptr) {
+// Launches `fn` with its parameter array; with `pdl` as the programmatic
+// dependent of the previous kernel on the stream (the kernels wait for it with
+// griddepcontrol.wait before reading the queries).
+cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint32_t smem, cudaStream_t stream,
+                          bool pdl) {
+  if (!pdl) return cudaLaunchKernel(fn, dim3((unsigned)blocks), dim3((unsigned)threads), params, smem, stream);
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, const kvf_exchange *x = nullptr,
+                      bool pdl = false) {
   TcLaunch L;
   cudaError_t e = plan_tc(a, sh, L);
   if (e != cudaSuccess) return e;
@@ -443,7 +464,7 @@ cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, c
   const kvf_args args = *a;
   const TcPlan plan = L.p;
   void *params[4] = {const_cast<kvf_args *>(&args), const_cast<TcPlan *>(&plan), &tk, &tv};
-  e = cudaLaunchKernel(L.fn, dim3((unsigned)L.blocks), dim3((unsigned)kTcThreads), params, L.p.smem_total, stream);
+  e = launch_params(L.fn, L.blocks, kTcThreads, params, L.p.smem_total, stream, pdl);
   if (e != cudaSuccess) return e;
   if (!L.p.final_out && !L.p.merge_in_kernel) e = launch_merge(a, sh.d, stream, true, x);
   return e != cudaSuccess ? e : cudaGetLastError();
@@ -458,7 +479,7 @@ namespace kvfb {
 namespace {
 
 cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path, cudaStream_t stream,
-                        const kvf_exchange *x) {
+                        const kvf_exchange *x, bool pdl = false) {
   Shape sh;
   cudaError_t e = check_args(a, fmt, d, g, ord, paged, sh);
   if (e != cudaSuccess) return e;
@@ -466,7 +487,7 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   e = resolve_path(sh, a->B * a->Hkv, path, kernel);
   if (e != cudaSuccess) return e;
   if (a->B == 0) return cudaSuccess;
-  if (kernel == 2) return launch_tc(a, sh, stream, x);
+  if (kernel == 2) return launch_tc(a, sh, stream, x, pdl);
   Launch L;
   e = plan_launch(a, sh, L);
   if (e != cudaSuccess) return e;
@@ -478,8 +499,7 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   const kvf_args args = *a;
   const Plan plan = L.p;
   void *params[4] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv};
-  e = cudaLaunchKernel(L.fn, dim3((unsigned)L.blocks), dim3((unsigned)L.threads), params,
-                       L.p.smem_total, stream);
+  e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl);
   if (e != cudaSuccess) return e;
   if (!L.p.final_out) e = launch_merge(a, d, stream, true, x);
   return e != cudaSuccess ? e : cudaGetLastError();
@@ -496,6 +516,55 @@ extern "C" cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g,
 extern "C" cudaError_t kvf_b200_decode_path(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path,
                                             cudaStream_t stream) {
   return decode_impl(a, fmt, d, g, ord, paged, path, stream, nullptr);
+}
+
+namespace kvfb {
+namespace {
+
+// Copies the queries from host memory the device can address into a->q:
+// one 16-byte load and store per thread (the host reads go over PCIe). The
+// decode grid that follows may start at once; it reads the queries after
+// griddepcontrol.wait.
+__global__ void __launch_bounds__(256) stage_in_kernel(float4 *dst, const float4 *src, long long n4) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n4) dst[i] = src[i];
+}
+
+// Host memory the kernels may read or write directly: pinned and mapped at
+// the same address (cudaHostAlloc under unified addressing), or device memory.
+bool device_addressable(const void *p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) return true;
+  return at.type == cudaMemoryTypeHost && at.devicePointer == p;
+}
+
+} // namespace
+} // namespace kvfb
+
+extern "C" cudaError_t kvf_b200_decode_from_host(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
+                                                 int path, const float *q_host, cudaStream_t stream) {
+  Shape sh;
+  cudaError_t e = check_args(a, fmt, d, g, ord, paged, sh);
+  if (e != cudaSuccess) return e;
+  if (a->B == 0) return cudaSuccess;
+  const long long n = (long long)a->B * a->H * d;
+  if (!q_host || (reinterpret_cast<uintptr_t>(q_host) & 15u) || (reinterpret_cast<uintptr_t>(a->q) & 15u) ||
+      (n & 3))
+    return cudaErrorInvalidValue;
+  if (!device_addressable(q_host) || !device_addressable(a->q) || !device_addressable(a->out) ||
+      (a->lse && !device_addressable(a->lse)))
+    return cudaErrorInvalidValue;
+  const long long n4 = n / 4;
+  stage_in_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<float4 *>(const_cast<float *>(a->q)), reinterpret_cast<const float4 *>(q_host), n4);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return decode_impl(a, fmt, d, g, ord, paged, path, stream, nullptr, true);
 }
 
 extern "C" cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,

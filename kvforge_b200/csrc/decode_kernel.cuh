@@ -386,6 +386,11 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   const int h = hgi * p.hh + warp;  // KV head of this warp
   const int g8 = lane >> 2;         // fragment row group
   const int c4 = lane & 3;          // thread in group
+  // When launched as the programmatic dependent of a kernel that stages the
+  // queries (kvf_b200_decode_from_host), the K/V stream above has already
+  // started; the queries are read only once that kernel has completed. A
+  // launch without that dependency returns here at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float *qbase = a.q + ((long long)b * a.H + (long long)h * p.gq) * D;
   constexpr float CENTRE = FMT == 1 ? kCentre8 : kCentre4;
 

@@ -169,6 +169,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   }
   __syncthreads();
   if (warp < NH) {
+    // Queries staged by a preceding kernel (kvf_b200_decode_from_host) are
+    // read only after it completed; without that dependency this returns at once.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     {
       const int hq = warp;
       const bool live = hq < p.gq;

@@ -370,3 +370,54 @@ def test_errors_surface_as_codes(cuda):
     a.v = a.v + 8
     assert lib().kvf_b200_decode(ctypes.byref(a), FMT_INT8, 128, 1, 0, 0, None) == 716
     assert api.device_errors() == 0
+
+
+@pytest.mark.parametrize("zero_copy", [True, False], ids=["zero_copy", "copies"])
+@pytest.mark.parametrize("fmt,group,place", [
+    (FMT_INT8, 64, Placement(ORD_TOKEN, False, 0)),
+    (FMT_F16, 0, Placement(ORD_HEAD, True, 16)),
+    (FMT_INT8, 128, Placement(ORD_TOKEN, True, 16)),
+], ids=["int8_tm", "f16_hm_p16", "int8_tm_p16"])
+def test_decoder_graph_replays_match_direct_decode(cuda, fmt, group, place, zero_copy):
+    """api.Decoder (one CUDA graph per step: queries from and output to pinned
+    host memory, with or without copy-engine transfers) gives what api.decode
+    gives, step after step, for new queries and a changed cache."""
+    rs = np.random.RandomState(31)
+    B, H, Hkv, D, n = 2, 16, 4, 128, 900
+    K = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    V = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    cache = api.KVCache.from_logical(K, V, fmt=fmt, group=group, place=place)
+    dec = api.Decoder(cache, H, splits=5, zero_copy=zero_copy)
+    assert dec.graph is not None
+    for step in range(3):
+        q = torch.as_tensor(rs.standard_normal((B, H, D)).astype(np.float32))
+        got = dec.step(q).clone()
+        want = api.decode(q.to(cuda), cache, splits=5).cpu()
+        assert torch.equal(got, want), step
+    # The graph reads the cache in place: new contents show up in the next step.
+    if fmt == FMT_F16:
+        cache.v.zero_()
+        assert torch.count_nonzero(dec.step(q)) == 0
+    assert api.device_errors() == 0
+
+
+def test_decode_from_host_rejects_pageable_buffers(cuda):
+    """Host buffers the device cannot address are refused before any launch."""
+    rs = np.random.RandomState(32)
+    K = torch.as_tensor(rs.standard_normal((1, 2, 64, 128)).astype(np.float32), device=cuda)
+    cache = api.KVCache.from_logical(K, K, fmt=FMT_F16, place=Placement(ORD_HEAD, False, 0))
+    qd = torch.zeros((1, 8, 128), dtype=torch.float32, device=cuda)
+    out = torch.zeros_like(qd)
+    ws = api.Workspace.allocate(1, 8, 128, 1, cuda)
+    a = api.make_args(qd, cache, out, ws)
+    pageable = np.zeros((1, 8, 128), dtype=np.float32)
+    pinned = torch.zeros((1, 8, 128), dtype=torch.float32).pin_memory()
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    f = lib().kvf_b200_decode_from_host
+    assert f(ctypes.byref(a), FMT_F16, 128, 1, ORD_HEAD, 0, 0, ctypes.c_void_p(pageable.ctypes.data), st) == 1
+    a.out = pageable.ctypes.data
+    assert f(ctypes.byref(a), FMT_F16, 128, 1, ORD_HEAD, 0, 0, ctypes.c_void_p(pinned.data_ptr()), st) == 1
+    a.out = out.data_ptr()
+    assert f(ctypes.byref(a), FMT_F16, 128, 1, ORD_HEAD, 0, 0, ctypes.c_void_p(pinned.data_ptr()), st) == 0
+    torch.cuda.synchronize()
+    assert api.device_errors() == 0
