@@ -397,7 +397,9 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
   const uint32_t qtile = (uint32_t)(ns * 128);
   const uint32_t misc = tc_misc_bytes(sh.gpr, L.nh);
   // 1024 bytes of slack for aligning the dynamic shared-memory base.
-  const uint32_t fixed = 1024u + ((qtile + 1023u) & ~1023u) + p.ptile_bytes + misc;
+  // The P' tile of a stage is written over its K tile (dead after the score
+  // MMAs), so it takes no shared memory of its own.
+  const uint32_t fixed = 1024u + ((qtile + 1023u) & ~1023u) + misc;
   int occ = 2, stages = 0;
   for (; occ >= 1; --occ) {
     const int budget = std::min(kSmemPerBlockMax, kSmemPerSM / occ - kReservedPerBlock) - (int)fixed;
@@ -408,8 +410,8 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
   L.occupancy = occ;
   p.stages = stages;
   p.off_q = (uint32_t)stages * p.stage_bytes;
-  p.off_p = p.off_q + ((qtile + 1023u) & ~1023u);
-  p.off_misc = p.off_p + p.ptile_bytes;
+  p.off_p = 0;
+  p.off_misc = p.off_q + ((qtile + 1023u) & ~1023u);
   p.smem_total = 1024u + p.off_misc + misc;
   uint32_t cols = (uint32_t)(2 * sh.gpr * ns + np);
   uint32_t alloc = 32;

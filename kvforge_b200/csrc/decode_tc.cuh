@@ -20,7 +20,8 @@
 //           the same way: scale * code + zero).
 //
 //   values  O^T[128 dims x cols] = V codes (u8, read MN-major from the same
-//           tile) * P' planes (u8), where P'_t = rint(p_t * vscale_t * 2^ev) is a
+//           tile) * P' planes (u8, written over the stage's K tile, which is
+//           dead once the score MMAs completed), where P'_t = rint(p_t * vscale_t * 2^ev) is a
 //           24-bit integer per (token, head, group) split into three byte planes;
 //           ev puts the stage's largest V scale in [2^23, 2^24). Each stage's
 //           exact product is folded into fp32 registers with the stage's
@@ -68,8 +69,8 @@ struct TcPlan {
   uint32_t stage_bytes;  // K tile, V tile (128 x 128 bytes each), K meta, V meta; 1024-aligned
   uint32_t meta_bytes;   // one metadata area: 128 rows x groups x 4 bytes, 128-aligned
   uint32_t off_q;        // Q plane tile: NS rows x 128 bytes, 128-byte swizzle
-  uint32_t off_p;        // P' tile (value MMA operand)
-  uint32_t ptile_bytes;
+  uint32_t off_p;        // unused: the P' tile of a stage lives in its K tile
+  uint32_t ptile_bytes;  // P' tile bytes (<= the K tile)
   uint32_t off_misc;     // scalars, exchange areas, barriers
   uint32_t tmem_cols;    // allocated tensor-memory columns
   uint32_t smem_total;
@@ -124,7 +125,6 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   const uint32_t bar_full = bars, bar_empty = bars + 64, bar_sfull = bars + 128, bar_sfree = bars + 144,
                  bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 176, bar_done = bars + 192;
   const uint32_t sq = sbase + p.off_q;
-  const uint32_t sp = sbase + p.off_p;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -358,11 +358,12 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         }
         if (npv < ns && ptx::mbar_test_wait(bar_pready, (uint32_t)(npv & 1))) {
           tc::fence_after();
-          const uint32_t sv = sbase + (uint32_t)(npv % p.stages) * p.stage_bytes + TB * 128u;
+          const uint32_t sk = sbase + (uint32_t)(npv % p.stages) * p.stage_bytes;  // P' tile of the stage
+          const uint32_t sv = sk + TB * 128u;
 #pragma unroll
           for (int ks = 0; ks < TB / 32; ++ks)
             tc::mma_i8(tbase + 2u * SC, tc::smem_desc(sv + ks * 4096u, 16384u, 1024u, tc::kSwizzle128),
-                       tc::smem_desc(sp + ks * 512u, 128u, 2048u, tc::kSwizzleNone), ID_V, ks > 0);
+                       tc::smem_desc(sk + ks * 512u, 128u, 2048u, tc::kSwizzleNone), ID_V, ks > 0);
           tc::commit(bar_ofull);
           tc::commit(bar_empty + 8u * (npv % p.stages));
           ++npv;
@@ -589,15 +590,18 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         }
       }
 
-      // ---- fold the previous stage's value product; after it the P' tile is
-      // free again (its value MMAs have completed).
+      // ---- fold the previous stage's value product; after it the value
+      // accumulator in tensor memory is free for this stage's product.
       if (i >= 1 && !fold(i - 1, aoprev)) {
         ok = false;
         break;
       }
 
       // ---- P' planes into the value operand tile (MN-major, 16-byte rows of
-      // 16 columns per 8-token core matrix).
+      // 16 columns per 8-token core matrix), over the stage's K tile: the
+      // score MMAs that read it completed (sfull above), and the slot is
+      // handed back to the producer only after the value MMAs.
+      const uint32_t sp = sbase + (uint32_t)(i % p.stages) * p.stage_bytes;
       const uint32_t rowoff = (uint32_t)(row >> 3) * 128u + (uint32_t)(row & 7) * 16u;
 #pragma unroll
       for (int g = 0; g < GPR; ++g) {
