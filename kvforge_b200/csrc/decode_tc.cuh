@@ -27,17 +27,20 @@
 //           exact product is folded into fp32 registers with the stage's
 //           rescale. The zero term sum_t p_t * vzero_t stays on the CUDA cores.
 //
-// Warp roles (320 threads, two blocks per SM):
+// Warp roles (352 threads, two blocks per SM):
 //   warps 0-7  warp w serves tensor-memory lanes 32(w%4) .. 32(w%4)+31 and half
 //              w/4 of the query heads: each thread owns one token (scores) and
 //              one dimension (output) for its heads. It reads the stage's
 //              scores from tensor memory, runs the online softmax in the log2
 //              domain with one rescale per stage, writes P' planes, and folds
 //              each stage's value product into fp32;
-//   warp 8     producer: TMA for the K and V tiles, cp.async for the per-row
-//              quantization metadata of the same tokens (counted on the same
-//              full barrier);
-//   warp 9     MMA issuer (one thread): issues each stage's score MMAs as soon
+//   warps 8-9  producers (warp 8 + j takes the stages i with i % 2 == j): TMA
+//              for the K and V tiles, cp.async for the per-row quantization
+//              metadata of the same tokens (counted on the same full barrier).
+//              One warp cannot issue a stage's copies (with small pages, 16
+//              TMA boxes and 256 metadata rows) as fast as the ring drains: it
+//              shares its sub-partition's issue slots with softmax warps;
+//   warp 10    MMA issuer (one thread): issues each stage's score MMAs as soon
 //              as its tiles land and each stage's value MMAs as soon as its P'
 //              planes are written, whichever comes first.
 // Columns of a quantization group g are ordered g*NS + half*NS/2 + plane*NH/2 +
@@ -77,7 +80,10 @@ struct TcPlan {
 };
 
 constexpr int kTcTokens = 128;  // tokens per stage (M of the score MMA)
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 352;     // 8 softmax warps, 2 producers, MMA issuer
+constexpr int kTcProducerWarp = 8;  // and 9
+constexpr int kTcProducers = 2;
+constexpr int kTcMmaWarp = 10;
 
 // Scalars, exchange areas and barriers in the misc region.
 template <int GPR, int NH> struct TcMisc {
@@ -89,6 +95,7 @@ template <int GPR, int NH> struct TcMisc {
   uint32_t tmem_base;
   int abort_flag;             // set by any warp that gave up; the others stop waiting
   int last;                   // this block is the last of its (sequence, KV head)
+  int slot_last[8];           // last stage whose copies went into each ring slot (-1: none)
   // full[8], empty[8], sfull[2], sfree[2], pready, ofull, red[2], done
   uint64_t bars[32];
 };
@@ -142,6 +149,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 
   if (tid == 0) {
     ms.abort_flag = 0;
+    for (int s = 0; s < 8; ++s) ms.slot_last[s] = -1;
     for (int s = 0; s < p.stages; ++s) {
       ptx::mbar_init(bar_full + 8u * s, 33u);  // expect_tx arrival + 32 cp.async arrivals
       ptx::mbar_init(bar_empty + 8u * s, 1u);
@@ -156,7 +164,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     ptx::mbar_init(bar_done, 1u);
     ptx::fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kTcMmaWarp) {
     tc::alloc(ptx::smem_u32(&ms.tmem_base), p.tmem_cols);
     tc::relinquish();
   }
@@ -226,8 +234,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   // The separate merge kernel (if any) may be scheduled now; it waits for this grid.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
+  if (warp >= kTcProducerWarp && warp < kTcProducerWarp + kTcProducers) {
+    // ----------------------------------------------------------- producers
+    const int pw = warp - kTcProducerWarp;
     if (lane == 0) {
       ptx::prefetch_tmap(&tmk);
       ptx::prefetch_tmap(&tmv);
@@ -244,10 +253,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
     }
     bool ok = true;
-    int issued = 0;
-    int s = 0;
-    uint32_t phase = 0;
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = pw; i < ntiles; i += kTcProducers) {
+      const int s = i % p.stages;
+      const uint32_t phase = (uint32_t)(i / p.stages) & 1u;
       if (i >= p.stages && !warp_wait(bar_empty + 8u * s, phase ^ 1u, abort_flag)) {
         ok = false;
         break;
@@ -309,24 +317,26 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         }
         ptx::cp_async_arrive(bar_full + 8u * s);
       }
-      issued = i + 1;
-      if (++s == p.stages) {
-        s = 0;
-        phase ^= 1u;
-      }
+      if (lane == 0) *reinterpret_cast<volatile int *>(&ms.slot_last[s]) = i;
       if (*abort_flag) break;
     }
     if (!ok) {
       if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
       *abort_flag = 1;
     }
-    // Never leave with copies in flight: wait (bounded) for the last stages.
-    for (int i = max(0, issued - p.stages); i < issued; ++i) {
-      volatile int never = 0;
-      if (!warp_wait(bar_full + 8u * (i % p.stages), (i / p.stages) & 1, &never) && lane == 0)
-        atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+    // Never leave with copies in flight: once both producers are done, wait
+    // (bounded) for the last stage put into each slot (no later stage reused
+    // the slot, so its barrier parity is current).
+    asm volatile("bar.sync 3, 64;" ::: "memory");
+    if (pw == 0) {
+      for (int s = 0; s < p.stages; ++s) {
+        const int last = *reinterpret_cast<volatile int *>(&ms.slot_last[s]);
+        volatile int never = 0;
+        if (last >= 0 && !warp_wait(bar_full + 8u * s, (uint32_t)(last / p.stages) & 1u, &never) && lane == 0)
+          atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+      }
     }
-  } else if (warp == 9) {
+  } else if (warp == kTcMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_S = tc::idesc_i8(false, true, false, false, 128, NS);
@@ -737,7 +747,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   }
 
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kTcMmaWarp) {
     tc::fence_after();
     tc::dealloc(tbase, p.tmem_cols);
   }
