@@ -246,11 +246,14 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     const int bmask = (1 << p.bt_shift) - 1;
     const int nblk_valid = p.paged ? min(a.max_blocks, (nb + bmask) >> p.bt_shift) : 0;
     const long long tab0 = (long long)b * a.max_blocks;
+    // Block-table window: pages of blocks [win, win + 96) in three registers
+    // per lane, loaded one window ahead of use.
     int win = p.paged ? (t0 >> p.bt_shift) : 0;
-    int pg_cur = 0, pg_nxt = 0;
+    int pg_cur = 0, pg_nxt = 0, pg_nn = 0;
     if (p.paged) {
       if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
       if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
+      if (win + 64 + lane < nblk_valid) pg_nn = __ldg(a.block_table + tab0 + win + 64 + lane);
     }
     bool ok = true;
     for (int i = pw; i < ntiles; i += kTcProducers) {
@@ -263,30 +266,31 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       const int tt = t0 + i * TB;
       const uint32_t sk = sbase + s * p.stage_bytes;
       const uint32_t sv = sk + TB * 128u;
-      int lanepage = 0;  // page of TMA box `lane` of this stage
+      int lanepage = 0;  // page of TMA box `lane` of this stage (lanes < npg)
       if (p.paged) {
-        for (int j = 0; j < p.npg; ++j) {
-          const int blk = (tt + (j << tbs)) >> p.bt_shift;
-          while (blk >= win + 32) {
-            win += 32;
-            pg_cur = pg_nxt;
-            pg_nxt = (win + 32 + lane < nblk_valid) ? __ldg(a.block_table + tab0 + win + 32 + lane) : 0;
-          }
-          const int pg = __shfl_sync(0xffffffffu, pg_cur, blk - win);
-          if (lane == j) lanepage = pg;
+        // Box j of the stage lies in block blk0 + j (several boxes per stage
+        // only when a page holds at most 128 tokens, one box per page).
+        const int blk0 = tt >> p.bt_shift;
+        while (blk0 >= win + 32) {
+          win += 32;
+          pg_cur = pg_nxt;
+          pg_nxt = pg_nn;
+          pg_nn = (win + 64 + lane < nblk_valid) ? __ldg(a.block_table + tab0 + win + 64 + lane) : 0;
         }
+        const int idx = blk0 - win + (lane < p.npg ? lane : 0);  // < 32 + 8
+        const int from_cur = __shfl_sync(0xffffffffu, pg_cur, idx & 31);
+        const int from_nxt = __shfl_sync(0xffffffffu, pg_nxt, idx & 31);
+        lanepage = idx < 32 ? from_cur : from_nxt;
       }
       if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, 2u * TB * 128u);
-      for (int j = 0; j < p.npg; ++j) {
-        const int pg = __shfl_sync(0xffffffffu, lanepage, j);
-        if (lane == 0) {
-          const int tok = tt + (j << tbs);
-          const int c1 = p.paged ? (tok & bmask) : tok;
-          const int c3 = p.paged ? pg : b;
-          const uint32_t off = (uint32_t)j * (uint32_t)(p.tbox * 128);
-          ptx::tma_g2s_4d(sk + off, &tmk, 0, c1, h, c3, bar_full + 8u * s, pol);
-          ptx::tma_g2s_4d(sv + off, &tmv, 0, c1, h, c3, bar_full + 8u * s, pol);
-        }
+      __syncwarp();
+      if (lane < p.npg) {  // lane j issues box j of K and of V
+        const int tok = tt + (lane << tbs);
+        const int c1 = p.paged ? (tok & bmask) : tok;
+        const int c3 = p.paged ? lanepage : b;
+        const uint32_t off = (uint32_t)lane * (uint32_t)(p.tbox * 128);
+        ptx::tma_g2s_4d(sk + off, &tmk, 0, c1, h, c3, bar_full + 8u * s, pol);
+        ptx::tma_g2s_4d(sv + off, &tmv, 0, c1, h, c3, bar_full + 8u * s, pol);
       }
       {
         // Metadata rows of the stage's tokens that lie inside the chunk.
