@@ -198,6 +198,25 @@ cudaError_t plan_launch(const kvf_args *a, const Shape &sh, Launch &L) {
   p.kv_bytes = (uint32_t)(p.tb * p.hh * rb);
   p.meta_bytes = (uint32_t)(p.tb * p.hh * sh.gpr * 4);
   p.tx_bytes = 2u * p.kv_bytes;
+  // Metadata by TMA for contiguous caches whose layout gives rows of >= 16
+  // bytes in a 3-D view (see decode_kernel.cuh); cp.async otherwise.
+  p.meta_tma = 0;
+  p.meta_ts = (uint32_t)(sh.gpr * 4);
+  p.meta_hs = (uint32_t)(p.tb * sh.gpr * 4);
+  if (sh.gpr > 0 && !sh.paged && (p.meta_bytes % 128u) == 0 &&
+      (reinterpret_cast<uintptr_t>(a->k_meta) & 15u) == 0 && (reinterpret_cast<uintptr_t>(a->v_meta) & 15u) == 0) {
+    const long long g4 = (long long)sh.gpr * 4;
+    const bool ok = sh.ord ? ((a->Hkv * g4) % 16 == 0 && (p.hh * g4) % 16 == 0)
+                           : (((long long)a->n * g4) % 16 == 0 && p.tb * sh.gpr <= 256 && (p.tb * g4) % 16 == 0);
+    if (ok) {
+      p.meta_tma = 1;
+      p.tx_bytes += 2u * p.meta_bytes;
+      if (sh.ord) {
+        p.meta_ts = (uint32_t)(p.hh * g4);
+        p.meta_hs = (uint32_t)g4;
+      }
+    }
+  }
   const uint32_t meta_al = (p.meta_bytes + 127u) & ~127u;
   p.stage_bytes = (2u * p.kv_bytes + 2u * meta_al + 1023u) & ~1023u;
   const int ng = sh.gpr > 0 ? sh.gpr : 1;
@@ -240,6 +259,43 @@ cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int 
 cudaError_t encode_maps(const kvf_args *a, const Shape &sh, const Plan &p, CUtensorMap &tk,
                         CUtensorMap &tv) {
   return encode_maps_box(a, sh, p.rb, p.boxx, p.tbox, p.hh, tk, tv);
+}
+
+// Tensor maps over the K and V metadata (32-bit words) of a contiguous cache:
+// token-major [B][n][Hkv * groups] with boxes of (hh * groups, tb, 1),
+// head-major [B][Hkv][n * groups] with boxes of (tb * groups, hh, 1).
+cudaError_t encode_meta_maps(const kvf_args *a, const Shape &sh, const Plan &p, CUtensorMap &tkm,
+                             CUtensorMap &tvm) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t g = (cuuint64_t)sh.gpr, n = (cuuint64_t)std::max(a->n, 1), H = (cuuint64_t)a->Hkv;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  if (sh.ord) {
+    dims[0] = H * g;
+    dims[1] = n;
+    strides[0] = H * g * 4;
+    box[0] = (cuuint32_t)(p.hh * sh.gpr);
+    box[1] = (cuuint32_t)p.tb;
+  } else {
+    dims[0] = n * g;
+    dims[1] = H;
+    strides[0] = n * g * 4;
+    box[0] = (cuuint32_t)(p.tb * sh.gpr);
+    box[1] = (cuuint32_t)p.hh;
+  }
+  dims[2] = (cuuint64_t)std::max(a->B, 1);
+  strides[1] = n * H * g * 4;
+  box[2] = 1u;
+  const cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = enc(&tkm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(a->k_meta), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  r = enc(&tvm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(a->v_meta), dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
 cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int boxx, int tbox, int heads,
@@ -493,14 +549,23 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   Launch L;
   e = plan_launch(a, sh, L);
   if (e != cudaSuccess) return e;
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv, tkm, tvm;
   e = encode_maps(a, sh, L.p, tk, tv);
   if (e != cudaSuccess) return e;
+  std::memset(&tkm, 0, sizeof(tkm));
+  std::memset(&tvm, 0, sizeof(tvm));
+  if (L.p.meta_tma && encode_meta_maps(a, sh, L.p, tkm, tvm) != cudaSuccess) {
+    // The metadata goes by cp.async after all.
+    L.p.meta_tma = 0;
+    L.p.tx_bytes = 2u * L.p.kv_bytes;
+    L.p.meta_ts = (uint32_t)(sh.gpr * 4);
+    L.p.meta_hs = (uint32_t)(L.p.tb * sh.gpr * 4);
+  }
   e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
   if (e != cudaSuccess) return e;
   const kvf_args args = *a;
   const Plan plan = L.p;
-  void *params[4] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv};
+  void *params[6] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv, &tkm, &tvm};
   e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl);
   if (e != cudaSuccess) return e;
   if (!L.p.final_out) e = launch_merge(a, d, stream, true, x);
@@ -628,9 +693,10 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
     const KernelInfo ki = info_for(L.fn);
     std::snprintf(buf, (size_t)buf_len,
                   "kernel=mma.sync grid=%d block=%d heads/block=%d tokens/stage=%d stages=%d stage_bytes=%u "
-                  "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d",
+                  "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d meta=%s",
                   L.blocks, L.threads, L.p.hh, L.p.tb, L.p.stages, L.p.stage_bytes, L.p.smem_total,
-                  L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out);
+                  L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out,
+                  sh.gpr == 0 ? "none" : L.p.meta_tma ? "tma" : "cp.async");
   }
   return cudaSuccess;
 }

@@ -13,9 +13,13 @@
 //    head/token major x contiguous/paged) into a ring of shared-memory stages
 //    guarded by full/empty mbarriers. The tiles land swizzled (128/64/32-byte
 //    swizzle matching the row size) so the ldmatrix reads below are free of
-//    bank conflicts. Per-row quantization metadata (4-16 bytes per row) is too
-//    small for TMA boxes and is fetched by all 32 lanes with cp.async, whose
-//    completion is counted on the same full barrier.
+//    bank conflicts. Per-row quantization metadata (4-16 bytes per row) of
+//    contiguous caches comes by TMA as well, one box per stage and K/V: a
+//    3-D view whose inner dimension folds the KV heads (token-major rows:
+//    the block's heads of one token are adjacent) or the tokens (head-major
+//    rows: one head's tokens are adjacent), so a box row is >= 16 bytes. Paged
+//    caches fetch it with cp.async from all 32 lanes, counted on the same
+//    full barrier.
 //
 //  * One consumer warp per KV head. Scores and the value product run on the
 //    tensor cores with mma.sync m16n8k16 (f16 in, fp32 accumulate), with the
@@ -77,7 +81,10 @@ struct Plan {
   uint32_t kv_bytes;    // K (or V) bytes in one stage
   uint32_t meta_bytes;  // K (or V) metadata bytes in one stage
   uint32_t stage_bytes; // one stage, 1024-aligned
-  uint32_t tx_bytes;    // TMA bytes expected per stage (K + V)
+  uint32_t tx_bytes;    // TMA bytes expected per stage (K + V, and their metadata by TMA)
+  int meta_tma;         // metadata by TMA (contiguous caches) instead of cp.async
+  uint32_t meta_ts;     // bytes between a head's consecutive tokens in a stage's metadata area
+  uint32_t meta_hs;     // bytes between the heads' first tokens there
   uint32_t off_bars;    // full[stages], empty[stages]
   uint32_t off_pscr;    // P^T scratch, pscr_warp bytes per consumer warp
   uint32_t pscr_warp;
@@ -209,7 +216,8 @@ template <int FMT, int D, int GPR, int NT>
 // blocks per SM.
 __global__ void __launch_bounds__(160, 2)
 decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMap tmk,
-              const __grid_constant__ CUtensorMap tmv) {
+              const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmkm,
+              const __grid_constant__ CUtensorMap tmvm) {
   constexpr int RB = row_bytes(FMT, D);
   constexpr int NCH = RB / 16;          // 16-byte chunks per row
   constexpr int KSTEPS = D / 16;        // MMA k-steps per row
@@ -251,7 +259,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   if (threadIdx.x == 0) {
     s_abort = 0;
     for (int s = 0; s < p.stages; ++s) {
-      ptx::mbar_init(bar_full + 8u * s, GPR > 0 ? 33u : 1u);
+      ptx::mbar_init(bar_full + 8u * s, (GPR > 0 && !p.meta_tma) ? 33u : 1u);
       ptx::mbar_init(bar_empty + 8u * s, (uint32_t)p.hh);
     }
     ptx::fence_barrier_init();
@@ -265,6 +273,10 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     if (lane == 0) {
       ptx::prefetch_tmap(&tmk);
       ptx::prefetch_tmap(&tmv);
+      if (GPR > 0 && p.meta_tma) {
+        ptx::prefetch_tmap(&tmkm);
+        ptx::prefetch_tmap(&tmvm);
+      }
     }
     const uint64_t pol = ptx::policy_evict_first();
     const int bmask = (1 << p.bt_shift) - 1;
@@ -292,7 +304,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
         if (lane == 0) *reinterpret_cast<volatile int *>(&s_tag[s]) = -1;
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar_full + 8u * s);
-        if (GPR > 0) ptx::mbar_arrive(bar_full + 8u * s);  // 32 more: the cp.async share
+        if (GPR > 0 && !p.meta_tma) ptx::mbar_arrive(bar_full + 8u * s);  // 32 more: the cp.async share
         ended = true;
         break;
       }
@@ -323,7 +335,20 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
           }
         }
       }
-      if (GPR > 0) {
+      if (GPR > 0 && p.meta_tma) {
+        // Metadata of the stage by TMA, counted in tx_bytes: token-major
+        // (group words of the block's heads, token, sequence) lands as
+        // [token][head][group]; head-major (token x group words, head,
+        // sequence) as [head][token][group].
+        if (lane == 0) {
+          const uint32_t smk = sv + p.kv_bytes;
+          const uint32_t smv = smk + p.meta_bytes;
+          const int x = p.tm ? h0 * GPR : cur * GPR;
+          const int y = p.tm ? cur : h0;
+          ptx::tma_g2s_3d(smk, &tmkm, x, y, b, bar_full + 8u * s, pol);
+          ptx::tma_g2s_3d(smv, &tmvm, x, y, b, bar_full + 8u * s, pol);
+        }
+      } else if (GPR > 0) {
         // Metadata rows (hh heads x TB tokens) of the stage's tokens.
         const uint32_t smk = sv + p.kv_bytes;
         const uint32_t smv = smk + p.meta_bytes;
@@ -494,8 +519,11 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
                    (((uint32_t)(ch % CPB) * 16u) ^ xorv);
     }
   }
-  // Metadata of (this warp's head, token t): words at meta + (warp*TB + t)*GPR*4.
-  const uint32_t meta_lane = (uint32_t)((warp * TB + g8) * GPR * 4);
+  // Metadata of (this warp's head, token t): words at meta + warp*hs + t*ts
+  // (hs = TB*GPR*4, ts = GPR*4 when [head][token][group]; hs = GPR*4,
+  // ts = hh*GPR*4 when [token][head][group]).
+  const uint32_t meta_ts = p.meta_ts;
+  const uint32_t meta_lane = (uint32_t)warp * p.meta_hs + (uint32_t)g8 * meta_ts;
 
   int s = 0;
   uint32_t phase = 0;
@@ -537,7 +565,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
 
       // Metadata words of this thread's tokens (rows g8, g8 + 8 of m-tile mt).
       auto load_meta = [&](uint32_t base, int mt, int rr, uint32_t (&w)[NG]) {
-        const uint32_t ad = base + meta_lane + (uint32_t)((mt * 16 + rr * 8) * GPR * 4);
+        const uint32_t ad = base + meta_lane + (uint32_t)(mt * 16 + rr * 8) * meta_ts;
         if (GPR == 1) {
           asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w[0]) : "r"(ad));
         } else if (GPR == 2) {
