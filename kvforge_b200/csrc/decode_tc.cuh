@@ -534,13 +534,17 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         red[e] = sc[e];
       }
       red[HT] = __uint_as_float(vbits);
+      // Warp maxima in one redux.sync each: scores through an order-preserving
+      // map of floats to unsigned integers (sign bit set for >= 0, all bits
+      // flipped for < 0), the V-scale bits as they are.
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-        for (int e = 0; e <= HT; ++e) {
-          const float o = __shfl_xor_sync(0xffffffffu, red[e], off);
-          red[e] = e < HT ? fmaxf(red[e], o) : __uint_as_float(max(__float_as_uint(red[e]), __float_as_uint(o)));
-        }
+      for (int e = 0; e <= HT; ++e) {
+        uint32_t u = __float_as_uint(red[e]);
+        if (e < HT) u = (int)u >= 0 ? (u | 0x80000000u) : ~u;
+        u = __reduce_max_sync(0xffffffffu, u);
+        if (e < HT) u = (int)u < 0 ? (u & 0x7FFFFFFFu) : ~u;
+        red[e] = __uint_as_float(u);
+      }
       if (lane == 0) {
 #pragma unroll
         for (int e = 0; e <= HT; ++e) ms.red[j][warp][e] = red[e];
