@@ -285,6 +285,16 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     const int h0 = hgi * p.hh;
     const uint32_t *kmeta = reinterpret_cast<const uint32_t *>(a.k_meta);
     const uint32_t *vmeta = reinterpret_cast<const uint32_t *>(a.v_meta);
+    // Block-table window: pages of blocks [win, win + 96) in three registers
+    // per lane, loaded one window ahead of use, so a stage's page lookup is
+    // two shuffles and never waits for memory.
+    int win = p.paged ? (t0 >> p.bt_shift) : 0;
+    int pg_cur = 0, pg_nxt = 0, pg_nn = 0;
+    if (p.paged) {
+      if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
+      if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
+      if (win + 64 + lane < nblk_valid) pg_nn = __ldg(a.block_table + tab0 + win + 64 + lane);
+    }
     // Stages to load: the chunk [t0, t1) in TB steps; each ring slot is tagged
     // with its first token, and a slot tagged -1 tells the consumers to stop.
     int tt = t0;
@@ -311,11 +321,22 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       if (lane == 0) *reinterpret_cast<volatile int *>(&s_tag[s]) = cur;
       const uint32_t sk = sbase + s * p.stage_bytes;
       const uint32_t sv = sk + p.kv_bytes;
-      // Page of TMA box `lane` of this stage (paged).
+      // Page of TMA box `lane` of this stage (paged): box j lies in block
+      // blk0 + j (several boxes per stage only when a page is shorter than
+      // a stage, one box per page).
       int lanepage = 0;
-      if (p.paged && lane < p.npg) {
-        const int blk = (cur + (lane << tbs)) >> p.bt_shift;
-        lanepage = blk < nblk_valid ? __ldg(a.block_table + tab0 + blk) : 0;
+      if (p.paged) {
+        const int blk0 = cur >> p.bt_shift;
+        while (blk0 >= win + 32) {
+          win += 32;
+          pg_cur = pg_nxt;
+          pg_nxt = pg_nn;
+          pg_nn = (win + 64 + lane < nblk_valid) ? __ldg(a.block_table + tab0 + win + 64 + lane) : 0;
+        }
+        const int idx = blk0 - win + (lane < p.npg ? lane : 0);  // < 32 + 4
+        const int from_cur = __shfl_sync(0xffffffffu, pg_cur, idx & 31);
+        const int from_nxt = __shfl_sync(0xffffffffu, pg_nxt, idx & 31);
+        lanepage = idx < 32 ? from_cur : from_nxt;
       }
       if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, p.tx_bytes);
 #pragma unroll
