@@ -492,20 +492,59 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
 // dependent of the previous kernel on the stream (the kernels wait for it with
 // griddepcontrol.wait before reading the queries).
 cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint32_t smem, cudaStream_t stream,
-                          bool pdl) {
-  if (!pdl) return cudaLaunchKernel(fn, dim3((unsigned)blocks), dim3((unsigned)threads), params, smem, stream);
+                          bool pdl, bool coop = false) {
+  if (!pdl && !coop) return cudaLaunchKernel(fn, dim3((unsigned)blocks), dim3((unsigned)threads), params, smem, stream);
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)blocks);
   cfg.blockDim = dim3((unsigned)threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (coop) {
+    attr[na].id = cudaLaunchAttributeCooperative;
+    attr[na].val.cooperative = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
   return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+// Whether a decode launch merges its splits itself (cooperative launch, grid
+// barrier): partials to merge, split counters with room for the barrier
+// words (two or more (sequence, KV head) units), every block resident at
+// once, and no programmatic dependency on a preceding kernel. It pays once the
+// separate merge kernel is large: measured on B200, 8 sequences with 1024
+// merge slices (query head x 32 columns) for 288 decode blocks step in 53.7 us
+// instead of 57.2, while single sequences with 128 slices for ~295 blocks
+// lose 1.4-2.5 us (the cooperative launch costs more than the merge kernel it
+// replaces). So by default it is used when there are at least two slices per
+// decode block; KVF_B200_COOP=1 forces it where possible, =0 never uses it.
+bool coop_merge_applies(const kvf_args *a, const Plan &p, int d, void *fn, int blocks, int threads, bool pdl) {
+  if (p.final_out || !a->split_sem || (long long)a->B * a->Hkv < 2 || pdl) return false;
+  const char *e = std::getenv("KVF_B200_COOP");
+  if (e && e[0] == '0') return false;
+  const bool forced = e && e[0] == '1';
+  const long long slices = (long long)a->B * a->H * ((d + 31) / 32);
+  if (!forced && slices < 2LL * blocks) return false;
+  int dev = 0, sms = 0, per_sm = 0;
+  // The occupancy of a block with this much dynamic shared memory counts only
+  // once the kernel may use it (set here too, so describing agrees with launching).
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_total) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, p.smem_total) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return blocks <= per_sm * sms;
 }
 
 cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, const kvf_exchange *x = nullptr,
@@ -563,12 +602,13 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   }
   e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
   if (e != cudaSuccess) return e;
+  L.p.coop_merge = (!x && coop_merge_applies(a, L.p, d, L.fn, L.blocks, L.threads, pdl)) ? 1 : 0;
   const kvf_args args = *a;
   const Plan plan = L.p;
   void *params[6] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv, &tkm, &tvm};
-  e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl);
+  e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl, L.p.coop_merge != 0);
   if (e != cudaSuccess) return e;
-  if (!L.p.final_out) e = launch_merge(a, d, stream, true, x);
+  if (!L.p.final_out && !L.p.coop_merge) e = launch_merge(a, d, stream, true, x);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -693,10 +733,12 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
     const KernelInfo ki = info_for(L.fn);
     std::snprintf(buf, (size_t)buf_len,
                   "kernel=mma.sync grid=%d block=%d heads/block=%d tokens/stage=%d stages=%d stage_bytes=%u "
-                  "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d meta=%s",
+                  "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d meta=%s merge=%s",
                   L.blocks, L.threads, L.p.hh, L.p.tb, L.p.stages, L.p.stage_bytes, L.p.smem_total,
                   L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out,
-                  sh.gpr == 0 ? "none" : L.p.meta_tma ? "tma" : "cp.async");
+                  sh.gpr == 0 ? "none" : L.p.meta_tma ? "tma" : "cp.async",
+                  L.p.final_out ? "none"
+                  : coop_merge_applies(a, L.p, d, L.fn, L.blocks, L.threads, false) ? "in-kernel(grid)" : "kernel");
   }
   return cudaSuccess;
 }

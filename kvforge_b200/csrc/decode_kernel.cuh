@@ -76,6 +76,7 @@ struct Plan {
   int tm;          // token-major rows (else head-major)
   int bt_shift;    // log2(tokens per page)
   int final_out;   // 1: write normalised out; 0: write partials
+  int coop_merge;  // cooperative launch: the blocks merge the splits after a grid barrier
   uint32_t swz;    // swizzle mask for the K/V tiles (0x70, 0x30, 0x10)
   uint32_t box_bytes;   // one TMA box
   uint32_t kv_bytes;    // K (or V) bytes in one stage
@@ -209,6 +210,86 @@ __device__ __forceinline__ int norm_exp(float m, int top) {
   int e = (int)((u >> 23) & 0xFFu) - 127;
   if (u & 0x7FFFFFu) e += 1;
   return top - e;
+}
+
+// Log-sum-exp merge of the split partials (runtime/kvf_kernels.cuh:288-306):
+//   M = max_s m_s,  L = sum_s l_s 2^(m_s - M),  out = sum_s o_s 2^(m_s - M) / L
+// (splits with m_s = -inf contribute nothing; L = 0 gives 0). One block per
+// (query head, sequence, 32 output columns); warp w takes splits w, w+8, ...,
+// issuing all of its loads before using any (one L2 round trip for up to
+// 256 splits), and the warps' partial (M, L, O) are combined the same way.
+constexpr int kMergeWarps = 8;
+constexpr int kMergeUnroll = 32;
+
+// Merged (M, L, O) of one (query head, 32-column slice) over all splits, for
+// warp 0 (lane = column); warps 0 .. nw-1 of the caller's block take part (a
+// block of kMergeWarps warps, or the consumer warps of a decode block, which
+// then synchronise on named barrier 1).
+struct MergeSmem {
+  float m[kMergeWarps], l[kMergeWarps];
+  float o[kMergeWarps][32];
+};
+
+__device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long head, int col, bool colok,
+                                             MergeSmem &sm, float &Mt, float &Lt, float &Ot, int nw = kMergeWarps) {
+  // kMergeWarps partial states, each over splits w, w + kMergeWarps, ...;
+  // warp i of the nw warps computes states i, i + nw, ..., so the arithmetic
+  // (and the result, bit for bit) is the same for any nw.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int S = a.splits;
+  const float *ml = a.part_ml + head * S * 2;
+  const float *po = a.part_o + head * (long long)S * d;
+
+  for (int vw = warp; vw < kMergeWarps; vw += nw) {
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int base = vw; base < S; base += kMergeWarps * kMergeUnroll) {
+      float ms[kMergeUnroll], ls[kMergeUnroll], os[kMergeUnroll];
+#pragma unroll
+      for (int k = 0; k < kMergeUnroll; ++k) {
+        const int sp = base + k * kMergeWarps;
+        const bool v = sp < S;
+        ms[k] = v ? __ldcg(ml + 2 * sp) : -INFINITY;
+        ls[k] = v ? __ldcg(ml + 2 * sp + 1) : 0.f;
+        os[k] = (v && colok) ? __ldcg(po + (long long)sp * d + col) : 0.f;
+      }
+      float mx = M;
+#pragma unroll
+      for (int k = 0; k < kMergeUnroll; ++k) mx = fmaxf(mx, ms[k]);
+      if (mx == -INFINITY) continue;
+      const float r = exp2f(M - mx);  // 0 when M is -inf
+      L *= r;
+      O *= r;
+#pragma unroll
+      for (int k = 0; k < kMergeUnroll; ++k) {
+        const float w = ms[k] == -INFINITY ? 0.f : exp2f(ms[k] - mx);
+        L = fmaf(ls[k], w, L);
+        O = fmaf(os[k], w, O);
+      }
+      M = mx;
+    }
+    if (lane == 0) {
+      sm.m[vw] = M;
+      sm.l[vw] = L;
+    }
+    sm.o[vw][lane] = O;
+  }
+  if (nw == kMergeWarps) __syncthreads();
+  else asm volatile("bar.sync 1, %0;" ::"r"(nw * 32) : "memory");
+  Mt = -INFINITY;
+  Lt = 0.f;
+  Ot = 0.f;
+  if (warp == 0) {
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, sm.m[w]);
+    if (Mt != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kMergeWarps; ++w) {
+        const float wt = sm.m[w] == -INFINITY ? 0.f : exp2f(sm.m[w] - Mt);
+        Lt = fmaf(sm.l[w], wt, Lt);
+        Ot = fmaf(sm.o[w][lane], wt, Ot);
+      }
+    }
+  }
 }
 
 template <int FMT, int D, int GPR, int NT>
@@ -868,7 +949,9 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
     s_abort = 1;
   }
-  if (!ok) return;
+  // With the in-launch merge every consumer warp takes part in the barriers
+  // below; a warp that gave up only skips its writes.
+  if (!ok && !p.coop_merge) return;
   // Reduce the per-thread sums over the 8 row groups.
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -884,7 +967,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int hq = nt * 4 + c4;
-    if (hq < p.gq) {
+    if (ok && hq < p.gq) {
       const long long head = (long long)b * a.H + (long long)h * p.gq + hq;
       const float L = l_run[nt];
       const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -912,76 +995,58 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       }
     }
   }
-}
 
-// Log-sum-exp merge of the split partials (runtime/kvf_kernels.cuh:288-306):
-//   M = max_s m_s,  L = sum_s l_s 2^(m_s - M),  out = sum_s o_s 2^(m_s - M) / L
-// (splits with m_s = -inf contribute nothing; L = 0 gives 0). One block per
-// (query head, sequence, 32 output columns); warp w takes splits w, w+8, ...,
-// issuing all of its loads before using any (one L2 round trip for up to
-// 256 splits), and the warps' partial (M, L, O) are combined the same way.
-constexpr int kMergeWarps = 8;
-constexpr int kMergeUnroll = 32;
-
-// Merged (M, L, O) of one (query head, 32-column slice) over all splits, for
-// warp 0 (lane = column); the caller's block has kMergeWarps warps.
-struct MergeSmem {
-  float m[kMergeWarps], l[kMergeWarps];
-  float o[kMergeWarps][32];
-};
-
-__device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long head, int col, bool colok,
-                                             MergeSmem &sm, float &Mt, float &Lt, float &Ot) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int S = a.splits;
-  const float *ml = a.part_ml + head * S * 2;
-  const float *po = a.part_o + head * (long long)S * d;
-
-  float M = -INFINITY, L = 0.f, O = 0.f;
-  for (int base = warp; base < S; base += kMergeWarps * kMergeUnroll) {
-    float ms[kMergeUnroll], ls[kMergeUnroll], os[kMergeUnroll];
-#pragma unroll
-    for (int k = 0; k < kMergeUnroll; ++k) {
-      const int sp = base + k * kMergeWarps;
-      const bool v = sp < S;
-      ms[k] = v ? __ldcg(ml + 2 * sp) : -INFINITY;
-      ls[k] = v ? __ldcg(ml + 2 * sp + 1) : 0.f;
-      os[k] = (v && colok) ? __ldcg(po + (long long)sp * d + col) : 0.f;
-    }
-    float mx = M;
-#pragma unroll
-    for (int k = 0; k < kMergeUnroll; ++k) mx = fmaxf(mx, ms[k]);
-    if (mx == -INFINITY) continue;
-    const float r = exp2f(M - mx);  // 0 when M is -inf
-    L *= r;
-    O *= r;
-#pragma unroll
-    for (int k = 0; k < kMergeUnroll; ++k) {
-      const float w = ms[k] == -INFINITY ? 0.f : exp2f(ms[k] - mx);
-      L = fmaf(ls[k], w, L);
-      O = fmaf(os[k], w, O);
-    }
-    M = mx;
-  }
-  if (lane == 0) {
-    sm.m[warp] = M;
-    sm.l[warp] = L;
-  }
-  sm.o[warp][lane] = O;
-  __syncthreads();
-  Mt = -INFINITY;
-  Lt = 0.f;
-  Ot = 0.f;
-  if (warp == 0) {
-#pragma unroll
-    for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, sm.m[w]);
-    if (Mt != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kMergeWarps; ++w) {
-        const float wt = sm.m[w] == -INFINITY ? 0.f : exp2f(sm.m[w] - Mt);
-        Lt = fmaf(sm.l[w], wt, Lt);
-        Ot = fmaf(sm.o[w][lane], wt, Ot);
+  if (p.coop_merge) {
+    // ---- the split merge inside this launch. A cooperative launch keeps
+    // every block resident, so the blocks may wait for each other: a grid
+    // barrier (arrival count, bounded wait; the last block to leave resets
+    // both counters to zero for the next launch), then block i merges the
+    // (query head, 32-column) slices i, i + grid, ... as merge_kernel does.
+    const int nthr = p.hh * 32;
+    __threadfence();
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    __shared__ int s_pass;
+    if (threadIdx.x == 0) {
+      unsigned *arrived = a.split_sem + 1, *departed = a.split_sem + 3;
+      const unsigned nblk = gridDim.x;
+      atomicAdd(arrived, 1u);
+      const uint64_t tw = ptx::globaltimer_ns();
+      int pass = 1;
+      for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(arrived) : "memory");
+        if (v >= nblk) break;
+        if (ptx::globaltimer_ns() - tw > 2000000000ull) {
+          pass = 0;
+          break;
+        }
+        __nanosleep(64);
       }
+      if (!pass) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+      if (atomicAdd(departed, 1u) == nblk - 1) {
+        *reinterpret_cast<volatile unsigned *>(arrived) = 0u;
+        *reinterpret_cast<volatile unsigned *>(departed) = 0u;
+      }
+      s_pass = pass && !s_abort;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    if (!s_pass) return;
+    __threadfence();
+    __shared__ MergeSmem msm;
+    const int nz = (D + 31) / 32;
+    const long long items = (long long)a.B * a.H * nz;
+    for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+      const long long head = it / nz;
+      const int zc = (int)(it - head * nz);
+      const int col = zc * 32 + lane;
+      const bool colok = col < D;
+      float Mt, Lt, Ot;
+      merge_splits(a, D, head, col, colok, msm, Mt, Lt, Ot, p.hh);
+      if (warp == 0) {
+        if (colok) a.out[head * D + col] = Lt > 0.f ? Ot / Lt : 0.f;
+        if (lane == 0 && zc == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // msm is reused by the next slice
     }
   }
 }

@@ -421,3 +421,30 @@ def test_decode_from_host_rejects_pageable_buffers(cuda):
     assert f(ctypes.byref(a), FMT_F16, 128, 1, ORD_HEAD, 0, 0, ctypes.c_void_p(pinned.data_ptr()), st) == 0
     torch.cuda.synchronize()
     assert api.device_errors() == 0
+
+
+@pytest.mark.parametrize("B,H,Hkv,n,fmt,group,place", [
+    (1, 32, 8, 3000, FMT_INT8, 64, Placement(ORD_TOKEN, False, 0)),
+    (6, 16, 4, 1500, FMT_F16, 0, Placement(ORD_TOKEN, True, 16)),
+], ids=["b1_int8_tm", "b6_f16_tm_p16"])
+def test_in_launch_grid_merge_equals_merge_kernel(cuda, monkeypatch, B, H, Hkv, n, fmt, group, place):
+    """The mma.sync kernel's split merge after a grid barrier (cooperative
+    launch) gives the merge kernel's result bit for bit, launch after launch
+    (its barrier counters return to zero)."""
+    rs = np.random.RandomState(41)
+    q = torch.as_tensor(rs.standard_normal((B, H, 128)).astype(np.float32), device=cuda)
+    K = torch.as_tensor(rs.standard_normal((B, Hkv, n, 128)).astype(np.float32), device=cuda)
+    V = torch.as_tensor(rs.standard_normal((B, Hkv, n, 128)).astype(np.float32), device=cuda)
+    cache = api.KVCache.from_logical(K, V, fmt=fmt, group=group, place=place)
+    ws = api.Workspace.allocate(B, H, 128, 7, cuda)
+    outs = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("KVF_B200_COOP", mode)
+        desc = api.describe(q, cache, ws, path="mma")
+        assert ("merge=in-kernel(grid)" in desc) == (mode == "1"), desc
+        for _ in range(3):
+            outs[mode] = api.decode(q, cache, workspace=ws, path="mma").clone()
+        torch.cuda.synchronize()
+        assert int(ws.split_sem.abs().sum()) == 0
+    assert torch.equal(outs["0"], outs["1"])
+    assert api.device_errors() == 0
