@@ -53,12 +53,15 @@ enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
  *   scale_log2   softmax scale * log2(e)
  *   seq_lens     [B] tokens of each sequence (each <= n); NULL = all n.
  *   split_sem    [B][Hkv][2] unsigned counters, zero before the first call
- *                and left zero by every call. When given (and splits > 1) on
- *                the tensor-core path, the last block of each (sequence, KV
- *                head) merges the split partials itself instead of a second
- *                kernel (part_o/part_ml are still written and read). NULL =
- *                the reference's two-launch scheme. Calls sharing one array
- *                must not overlap on the GPU.
+ *                and left zero by every call. When given (and splits > 1)
+ *                the split merge runs inside the decode launch instead of a
+ *                second kernel (part_o/part_ml are still written and read):
+ *                on the tensor-core path the last block of each (sequence,
+ *                KV head) merges (counter word 2u of unit u); on the mma.sync
+ *                path, for batches with at least two merge slices per block,
+ *                a cooperative launch merges after a grid barrier (words 1
+ *                and 3). NULL = the reference's two-launch scheme. Calls
+ *                sharing one array must not overlap on the GPU.
  *   lse          [B][H] fp32, optional (NULL = not written): log2 of the
  *                softmax denominator of each query head, in the same units as
  *                part_ml (max + log2(sum)); -inf for a head with no tokens.
