@@ -112,14 +112,15 @@ int heads_per_block(int Hkv, int fmt, int d) {
   return 1;
 }
 
-template <int FMT, int D, int GPR, int NT> struct K {
-  static void *fn() { return reinterpret_cast<void *>(&decode_kernel<FMT, D, GPR, NT>); }
+template <int FMT, int D, int GPR, int NT, bool LEAN> struct K {
+  static void *fn() { return reinterpret_cast<void *>(&decode_kernel<FMT, D, GPR, NT, LEAN>); }
 };
 
-// Kernel for (fmt, d, gpr, nt); nullptr for an unsupported combination.
-void *kernel_for(int fmt, int d, int gpr, int nt) {
+// Kernel for (fmt, d, gpr, nt, lean); nullptr for an unsupported combination.
+void *kernel_for(int fmt, int d, int gpr, int nt, bool lean) {
 #define KVFB_CASE(F, DD, G, N)                                                     \
-  if (fmt == F && d == DD && gpr == G && nt == N) return K<F, DD, G, N>::fn();
+  if (fmt == F && d == DD && gpr == G && nt == N)                                  \
+    return lean ? K<F, DD, G, N, true>::fn() : K<F, DD, G, N, false>::fn();
 #define KVFB_NT(F, DD, G) KVFB_CASE(F, DD, G, 1) KVFB_CASE(F, DD, G, 2)
   KVFB_NT(0, 128, 0) KVFB_NT(0, 64, 0)
   KVFB_NT(1, 128, 1) KVFB_NT(1, 128, 2) KVFB_NT(1, 64, 1)
@@ -171,12 +172,12 @@ struct Launch {
   int occupancy = 0;
 };
 
-cudaError_t plan_launch(const kvf_args *a, const Shape &sh, Launch &L) {
+cudaError_t plan_launch(const kvf_args *a, const Shape &sh, Launch &L, bool lean) {
   Plan &p = L.p;
   std::memset(&p, 0, sizeof(p));
   const int gq = a->H / a->Hkv;
   const int nt = gq <= 4 ? 1 : 2;
-  L.fn = kernel_for(sh.fmt, sh.d, sh.gpr, nt);
+  L.fn = kernel_for(sh.fmt, sh.d, sh.gpr, nt, lean);
   if (!L.fn) return cudaErrorInvalidValue;
   p.gq = gq;
   p.gpr = sh.gpr;
@@ -517,30 +518,36 @@ cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 
-// Whether a decode launch merges its splits itself (cooperative launch, grid
-// barrier): partials to merge, split counters with room for the barrier
-// words (two or more (sequence, KV head) units), every block resident at
-// once, and no programmatic dependency on a preceding kernel. It pays once the
-// separate merge kernel is large: measured on B200, 8 sequences with 1024
-// merge slices (query head x 32 columns) for 288 decode blocks step in 53.7 us
-// instead of 57.2, while single sequences with 128 slices for ~295 blocks
-// lose 1.4-2.5 us (the cooperative launch costs more than the merge kernel it
-// replaces). So by default it is used when there are at least two slices per
-// decode block; KVF_B200_COOP=1 forces it where possible, =0 never uses it.
-bool coop_merge_applies(const kvf_args *a, const Plan &p, int d, void *fn, int blocks, int threads, bool pdl) {
-  if (p.final_out || !a->split_sem || (long long)a->B * a->Hkv < 2 || pdl) return false;
+// Whether a decode launch should merge its splits itself (cooperative launch,
+// grid barrier): partials to merge, split counters with room for the barrier
+// words (two or more (sequence, KV head) units), no programmatic dependency
+// on a preceding kernel. It pays once the separate merge kernel is large:
+// measured on B200, 8 sequences with 1024 merge slices (query head x 32
+// columns) for 288 decode blocks step in 53.7 us instead of 57.2, while
+// single sequences with 128 slices for ~295 blocks lose 1.4-2.5 us (the
+// cooperative launch costs more than the merge kernel it replaces). So by
+// default it is used from two slices per decode block; KVF_B200_COOP=1
+// forces it where possible, =0 never uses it.
+bool coop_wanted(const kvf_args *a, int d, int hh, bool pdl) {
+  if (a->splits <= 1 || !a->split_sem || (long long)a->B * a->Hkv < 2 || pdl) return false;
   const char *e = std::getenv("KVF_B200_COOP");
   if (e && e[0] == '0') return false;
-  const bool forced = e && e[0] == '1';
+  if (e && e[0] == '1') return true;
+  const long long blocks = (long long)a->B * (a->Hkv / std::max(1, hh)) * a->splits;
   const long long slices = (long long)a->B * a->H * ((d + 31) / 32);
-  if (!forced && slices < 2LL * blocks) return false;
+  return slices >= 2LL * blocks;
+}
+
+// Whether every block of the launch can be resident at once (required by a
+// cooperative launch).
+bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
   int dev = 0, sms = 0, per_sm = 0;
   // The occupancy of a block with this much dynamic shared memory counts only
   // once the kernel may use it (set here too, so describing agrees with launching).
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_total) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, p.smem_total) != cudaSuccess) {
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
@@ -585,8 +592,11 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   if (e != cudaSuccess) return e;
   if (a->B == 0) return cudaSuccess;
   if (kernel == 2) return launch_tc(a, sh, stream, x, pdl);
+  // The in-launch merge needs the general kernel; contiguous caches without
+  // it run the lean one.
+  const bool want_coop = !x && coop_wanted(a, d, heads_per_block(a->Hkv, fmt, d), pdl);
   Launch L;
-  e = plan_launch(a, sh, L);
+  e = plan_launch(a, sh, L, !sh.paged && !want_coop);
   if (e != cudaSuccess) return e;
   CUtensorMap tk, tv, tkm, tvm;
   e = encode_maps(a, sh, L.p, tk, tv);
@@ -602,7 +612,7 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   }
   e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
   if (e != cudaSuccess) return e;
-  L.p.coop_merge = (!x && coop_merge_applies(a, L.p, d, L.fn, L.blocks, L.threads, pdl)) ? 1 : 0;
+  L.p.coop_merge = (want_coop && !L.p.final_out && coop_fits(L.fn, L.blocks, L.threads, L.p.smem_total)) ? 1 : 0;
   const kvf_args args = *a;
   const Plan plan = L.p;
   void *params[6] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv, &tkm, &tvm};
@@ -726,8 +736,9 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
     }
     return cudaSuccess;
   }
+  const bool want_coop = coop_wanted(a, d, heads_per_block(a->Hkv, fmt, d), false);
   Launch L;
-  e = plan_launch(a, sh, L);
+  e = plan_launch(a, sh, L, !sh.paged && !want_coop);
   if (e != cudaSuccess) return e;
   if (buf && buf_len > 0) {
     const KernelInfo ki = info_for(L.fn);
@@ -738,7 +749,7 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
                   L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out,
                   sh.gpr == 0 ? "none" : L.p.meta_tma ? "tma" : "cp.async",
                   L.p.final_out ? "none"
-                  : coop_merge_applies(a, L.p, d, L.fn, L.blocks, L.threads, false) ? "in-kernel(grid)" : "kernel");
+                  : want_coop && coop_fits(L.fn, L.blocks, L.threads, L.p.smem_total) ? "in-kernel(grid)" : "kernel");
   }
   return cudaSuccess;
 }
@@ -798,7 +809,7 @@ extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, in
       if (plan_tc(&a, sh, T) == cudaSuccess) occ = T.occupancy;
     } else {
       Launch L;
-      if (group_ok(fmt, d, group) && H / Hkv <= 8 && plan_launch(&a, sh, L) == cudaSuccess) occ = L.occupancy;
+      if (group_ok(fmt, d, group) && H / Hkv <= 8 && plan_launch(&a, sh, L, !paged) == cudaSuccess) occ = L.occupancy;
     }
     cudaGetLastError();
   }

@@ -292,7 +292,10 @@ __device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long
   }
 }
 
-template <int FMT, int D, int GPR, int NT>
+// LEAN: a contiguous cache without the in-launch split merge; the block-table
+// and grid-barrier code is compiled out (it costs the contiguous launches
+// 1-3 % even when it does not run).
+template <int FMT, int D, int GPR, int NT, bool LEAN>
 // At most 4 KV heads (4 consumer warps + 1 producer warp) per block, two
 // blocks per SM.
 __global__ void __launch_bounds__(160, 2)
@@ -369,12 +372,15 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     // Block-table window: pages of blocks [win, win + 96) in three registers
     // per lane, loaded one window ahead of use, so a stage's page lookup is
     // two shuffles and never waits for memory.
-    int win = p.paged ? (t0 >> p.bt_shift) : 0;
+    int win = 0;
     int pg_cur = 0, pg_nxt = 0, pg_nn = 0;
-    if (p.paged) {
-      if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
-      if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
-      if (win + 64 + lane < nblk_valid) pg_nn = __ldg(a.block_table + tab0 + win + 64 + lane);
+    if constexpr (!LEAN) {
+      if (p.paged) {
+        win = t0 >> p.bt_shift;
+        if (win + lane < nblk_valid) pg_cur = __ldg(a.block_table + tab0 + win + lane);
+        if (win + 32 + lane < nblk_valid) pg_nxt = __ldg(a.block_table + tab0 + win + 32 + lane);
+        if (win + 64 + lane < nblk_valid) pg_nn = __ldg(a.block_table + tab0 + win + 64 + lane);
+      }
     }
     // Stages to load: the chunk [t0, t1) in TB steps; each ring slot is tagged
     // with its first token, and a slot tagged -1 tells the consumers to stop.
@@ -406,7 +412,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       // blk0 + j (several boxes per stage only when a page is shorter than
       // a stage, one box per page).
       int lanepage = 0;
-      if (p.paged) {
+      if (!LEAN && p.paged) {
         const int blk0 = cur >> p.bt_shift;
         while (blk0 >= win + 32) {
           win += 32;
@@ -951,7 +957,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   }
   // With the in-launch merge every consumer warp takes part in the barriers
   // below; a warp that gave up only skips its writes.
-  if (!ok && !p.coop_merge) return;
+  if (!ok && (LEAN || !p.coop_merge)) return;
   // Reduce the per-thread sums over the 8 row groups.
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -996,6 +1002,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     }
   }
 
+  if constexpr (!LEAN) {
   if (p.coop_merge) {
     // ---- the split merge inside this launch. A cooperative launch keeps
     // every block resident, so the blocks may wait for each other: a grid
@@ -1048,6 +1055,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       }
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // msm is reused by the next slice
     }
+  }
   }
 }
 
