@@ -29,6 +29,7 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 
 from . import costmodel
+from .codegen import variant_id
 
 FIELDS = ["name", "B", "H", "Hkv", "d", "n", "fmt", "group", "order", "paged", "block_tokens", "tokens",
           "splits", "path", "variant", "payload_bytes", "us", "us_min", "predicted_us", "suggested"]
@@ -122,7 +123,6 @@ def run(out: Path, quick: bool = False, reps: int = 15, warmup: int = 3, max_spl
                 errs = api.device_errors()
                 if errs:
                     raise RuntimeError(f"{name} splits={s} path={path}: device error bits {errs:#x}")
-                from .codegen import variant_id
 
                 rows.append({
                     "name": name, "B": w.B, "H": w.H, "Hkv": w.Hkv, "d": w.d, "n": w.n, "fmt": w.fmt,
