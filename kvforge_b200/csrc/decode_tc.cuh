@@ -96,7 +96,7 @@ template <int GPR, int NH> struct TcMisc {
   int abort_flag;             // set by any warp that gave up; the others stop waiting
   int last;                   // this block is the last of its (sequence, KV head)
   int slot_last[8];           // last stage whose copies went into each ring slot (-1: none)
-  // full[8], empty[8], sfull[2], sfree[2], pready, ofull, red[2], done
+  // full[8], empty[8], sfull[2], sfree[2], pready, ofull, red[2 parities][2 halves], done
   uint64_t bars[32];
 };
 
@@ -130,7 +130,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   volatile int *abort_flag = &ms.abort_flag;
   const uint32_t bars = ptx::smem_u32(&ms.bars[0]);
   const uint32_t bar_full = bars, bar_empty = bars + 64, bar_sfull = bars + 128, bar_sfree = bars + 144,
-                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 176, bar_done = bars + 192;
+                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 176, bar_done = bars + 208;
   const uint32_t sq = sbase + p.off_q;
 
   const int warp = threadIdx.x >> 5;
@@ -157,7 +157,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     for (int j = 0; j < 2; ++j) {
       ptx::mbar_init(bar_sfull + 8u * j, 1u);
       ptx::mbar_init(bar_sfree + 8u * j, 8u);
-      ptx::mbar_init(bar_red + 8u * j, 8u);
+      // Each half's four warps cover all 128 tokens of a stage, so a half
+      // exchanges its maxima (and the stage's V-scale maximum) on its own.
+      for (int hf = 0; hf < 2; ++hf) ptx::mbar_init(bar_red + 8u * (2 * j + hf), 4u);
     }
     ptx::mbar_init(bar_pready, 8u);
     ptx::mbar_init(bar_ofull, 1u);
@@ -548,13 +550,13 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       if (lane == 0) {
 #pragma unroll
         for (int e = 0; e <= HT; ++e) ms.red[j][warp][e] = red[e];
-        ptx::mbar_arrive(bar_red + 8u * j);
+        ptx::mbar_arrive(bar_red + 8u * (2 * j + half));
       }
-      if (!warp_wait(bar_red + 8u * j, (uint32_t)((i >> 1) & 1), abort_flag)) {
+      if (!warp_wait(bar_red + 8u * (2 * j + half), (uint32_t)((i >> 1) & 1), abort_flag)) {
         ok = false;
         break;
       }
-      // Head maxima over the four warps of this half; V-scale maximum over all.
+      // Head and V-scale maxima over the four warps of this half (all tokens).
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
         float v = ms.red[j][half * 4][e];
@@ -564,7 +566,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       }
       uint32_t vmax = 0;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) vmax = max(vmax, __float_as_uint(ms.red[j][w][HT]));
+      for (int w = 0; w < 4; ++w) vmax = max(vmax, __float_as_uint(ms.red[j][half * 4 + w][HT]));
 
       // ---- online softmax, one rescale per stage; P' as 24-bit integers
       const int ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vmax)), 24), 100), -100);
