@@ -4,8 +4,10 @@
 
 One JSON line on rank 0. A "step" is one decode step of one layer over the
 workload's KV cache (the kernel plus the split merge), with L2 flushed before
-every step (a write of 3 x L2), as the reference times it
-(runtime/kvf_host.h:302-330). The payload is 2 * rows * (row bytes + 4 * groups)
+every step: a write of 3 x L2, as the reference times it
+(runtime/kvf_host.h:302-330), then a read of 3 x L2 from a second buffer, so
+that the step does not also write the flush's dirty lines back to HBM (the
+line's "write_flush" gives the step after the write alone). The payload is 2 * rows * (row bytes + 4 * groups)
 (runtime/kvf_driver.cu:51) over the stored tokens; value = payload of all
 ranks / max-over-ranks step time, in TB/s.
 
@@ -281,7 +283,7 @@ def main():
     from kvforge_b200 import workloads
 
     wname = args.workload or workloads.HEADLINE
-    w = workloads.CONFIGS[wname]
+    w = workloads.WORKLOADS[wname]
     if args.batch:
         import dataclasses
 
@@ -298,7 +300,7 @@ def main():
 
     import torch
 
-    from kvforge_b200 import api
+    from kvforge_b200 import api, l2flush
     from kvforge_b200._native import check, lib
 
     dev = torch.device("cuda", local)
@@ -374,16 +376,15 @@ def main():
         merge_in_kernel = "merge=in-kernel" in desc
         launches_per_step = 1 if splits <= 1 or merge_in_kernel else 2
 
-    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    flush = torch.empty(max(96 << 20, 3 * l2), dtype=torch.uint8, device=dev)
+    flush = l2flush.L2Flush(dev)
     align_buf = torch.zeros(1, device=dev)
 
-    def prepare(i):
+    def prepare(i, clean=True):
         """Untimed before every step: the L2 flush and, with several ranks, a
         device-side all-reduce so that every rank starts the step together
         (a cross-GPU step is as fast as its slowest rank; without this the
         skew between the ranks' flushes would be timed)."""
-        flush.fill_(i & 0xFF)
+        flush(i, clean)
         if world > 1:
             import torch.distributed as dist
 
@@ -411,6 +412,21 @@ def main():
     ms_med = statistics.median(times_ms)
     ms_all = max_over_ranks(ms, world)
     errs = api.device_errors()
+
+    # ---- the same steps after the reference's flush alone (a write of
+    # 3 x L2, runtime/kvf_host.h:310): the step then also writes the flush's
+    # dirty lines back to HBM.
+    evw = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        prepare(i, clean=False)
+        evw[i][0].record(stream)
+        launch()
+        evw[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    wf_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evw), world)
 
     # ---- with the output all-gather (KV-head sharding only)
     gather_ms = None
@@ -486,7 +502,7 @@ def main():
             "data": "synthetic (seeded N(0,1) on device)",
             "config": w.config() | {"splits": splits, "payload_bytes_per_gpu": payload,
                                     "payload_bytes_total": total_payload,
-                                    "l2": "flushed before every step (3 x L2 write)",
+                                    "l2": l2flush.DESCRIPTION,
                                     "rank_alignment": ("device-side all-reduce before every step, untimed"
                                                        if world > 1 else None),
                                     "parallelism": parallelism},
@@ -503,6 +519,8 @@ def main():
             "clocks": clk.record(),
             "device_errors": errs,
         }
+        line["write_flush"] = {"us_per_step": wf_ms * 1e3, "value": total_payload / (wf_ms * 1e-3) / 1e12,
+                               "unit": "TB/s", "l2": "the reference's flush alone: a write of 3 x L2"}
         if gather_ms is not None:
             line["with_output_gather"] = {"us_per_step": gather_ms * 1e3,
                                           "value": total_payload / (gather_ms * 1e-3) / 1e12, "unit": "TB/s"}

@@ -46,7 +46,12 @@ enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
  *   part_o       [B][H][splits][D] fp32 workspace, used when splits > 1
  *   part_ml      [B][H][splits][2] fp32 workspace (running max in log2 units,
  *                running sum), used when splits > 1
- *   splits       partitions of each sequence's tokens (>= 1)
+ *   splits       partitions of each sequence's tokens (>= 1). With seq_lens
+ *                given, the mma.sync path balances the tokens over one wave
+ *                of blocks: every sequence uses the same chunk of tokens, so
+ *                a long sequence gets more splits than a short one, and
+ *                splits is then the most any sequence may use (the
+ *                workspace's capacity; kvf_b200_suggest_splits_ragged).
  *   warps        reference tuning knob; accepted and ignored on sm_100a
  *   group_shift  log2(quantization group), quantized formats
  *   block_shift  log2(tokens per page), paged layouts
@@ -235,6 +240,22 @@ const char *kvf_b200_variant_name(int i);
  * n is the longest sequence. Always >= 1. */
 int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group, int paged,
                             int block_tokens);
+/* The split count (workspace capacity per sequence) for a batch whose
+ * sequences may differ in length (seq_lens given): as many splits as one
+ * sequence can use under balanced splits, within 64 MiB of partials; the
+ * same as kvf_b200_suggest_splits where the launch does not balance
+ * (tensor-core path, or more (sequence, head group) units than one wave of
+ * blocks). Environment: KVF_B200_BALANCE=0 turns balancing off. */
+int kvf_b200_suggest_splits_ragged(int B, int H, int Hkv, int n, int fmt, int d, int group, int paged,
+                                   int block_tokens);
+/* The chunk (tokens per split) a balanced launch uses, computed on the host
+ * from host seq_lens exactly as the kernels compute it on the device: the
+ * smallest multiple of gran, at least ceil(n / splits), for which
+ * units * sum_b ceil(seq_lens[b] / chunk) <= grid (units: head groups per
+ * sequence; grid: blocks launched, as kvf_b200_describe reports them). -1
+ * for invalid arguments or units * B > grid. For sizing and tests; the
+ * launch itself never reads seq_lens on the host. */
+int kvf_b200_balanced_chunk(const int *seq_lens, int B, int n, int splits, int units, int grid, int gran);
 
 /* Writes a one-line description of the launch kvf_b200_decode would make
  * (grid, block, stages, tokens per stage, shared memory) into buf. Returns

@@ -92,6 +92,8 @@ SIGNATURES = [
     ("kvf_b200_variant_count", c_int, []),
     ("kvf_b200_variant_name", c_char_p, [c_int]),
     ("kvf_b200_suggest_splits", c_int, [c_int] * 9),
+    ("kvf_b200_suggest_splits_ragged", c_int, [c_int] * 9),
+    ("kvf_b200_balanced_chunk", c_int, [c_void_p] + [c_int] * 6),
     ("kvf_b200_describe", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_char_p, c_int]),
     ("kvf_b200_describe_path", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_char_p, c_int]),
     ("kvf_b200_device_errors", c_uint, []),

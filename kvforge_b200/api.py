@@ -161,9 +161,11 @@ class Workspace:
 
 
 def suggest_splits(cache: KVCache, H: int) -> int:
+    """Split count for decoding this cache: the launcher's own choice, or for a
+    cache with per-sequence lengths the capacity the balanced launch needs."""
     bt = cache.place.block_tokens if cache.place.paged else 0
-    return int(lib().kvf_b200_suggest_splits(cache.B, H, cache.Hkv, cache.n, cache.fmt, cache.d,
-                                             cache.group, int(cache.place.paged), bt))
+    fn = lib().kvf_b200_suggest_splits_ragged if cache.seq_lens is not None else lib().kvf_b200_suggest_splits
+    return int(fn(cache.B, H, cache.Hkv, cache.n, cache.fmt, cache.d, cache.group, int(cache.place.paged), bt))
 
 
 def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace) -> KvfArgs:

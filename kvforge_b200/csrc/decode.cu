@@ -339,7 +339,8 @@ cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int 
   return cudaSuccess;
 }
 
-cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl, const kvf_exchange *x = nullptr) {
+cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl, const kvf_exchange *x = nullptr,
+                         MergeBalance bal = MergeBalance{0, 0, 0}) {
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)a->H, (unsigned)a->B, (unsigned)((d + 31) / 32));
@@ -356,7 +357,7 @@ cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl, co
     const kvf_exchange xc = *x;
     return cudaLaunchKernelEx(&cfg, merge_exchange_kernel, args, d, xc);
   }
-  return cudaLaunchKernelEx(&cfg, merge_kernel, args, d);
+  return cudaLaunchKernelEx(&cfg, merge_kernel, args, d, bal);
 }
 
 
@@ -528,12 +529,11 @@ cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint
 // cooperative launch costs more than the merge kernel it replaces). So by
 // default it is used from two slices per decode block; KVF_B200_COOP=1
 // forces it where possible, =0 never uses it.
-bool coop_wanted(const kvf_args *a, int d, int hh, bool pdl) {
+bool coop_wanted(const kvf_args *a, int d, long long blocks, bool pdl) {
   if (a->splits <= 1 || !a->split_sem || (long long)a->B * a->Hkv < 2 || pdl) return false;
   const char *e = std::getenv("KVF_B200_COOP");
   if (e && e[0] == '0') return false;
   if (e && e[0] == '1') return true;
-  const long long blocks = (long long)a->B * (a->Hkv / std::max(1, hh)) * a->splits;
   const long long slices = (long long)a->B * a->H * ((d + 31) / 32);
   return slices >= 2LL * blocks;
 }
@@ -552,6 +552,53 @@ bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
     return false;
   }
   return blocks <= per_sm * sms;
+}
+
+// Streaming multiprocessors of the current device (148 when it cannot be asked).
+int sm_count() {
+  static std::atomic<int> cache[16];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (dev >= 0 && dev < 16) {
+    const int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+    cudaGetLastError();
+    v = 148;
+  }
+  if (dev >= 0 && dev < 16) cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+// The mma.sync launch: plan, token-balanced splits, in-launch merge.
+//
+// When seq_lens is given (sequences may differ in length) and every
+// (sequence, head group) fits in one wave of blocks, the grid is one wave
+// (blocks per SM x SMs, or fewer when the splits need fewer) and the blocks
+// share the tokens evenly (balanced_chunk in decode_kernel.cuh). With one
+// split count for all, a batch of 8 sequences of 2k-8k tokens kept 184 of
+// 296 block slots busy, each block reading up to 464 tokens; balanced, 296
+// blocks read at most ~336. The in-launch merge and the balanced splits need
+// the general kernel; contiguous caches without either run the lean one.
+cudaError_t plan_mma(const kvf_args *a, const Shape &sh, int d, bool pdl, const kvf_exchange *x, Launch &L,
+                     bool &want_coop) {
+  const int hh = heads_per_block(a->Hkv, sh.fmt, sh.d);
+  const char *env = std::getenv("KVF_B200_BALANCE");  // 0: one split count for all sequences
+  const bool bal_wanted = !x && a->seq_lens && a->splits > 1 && !(env && env[0] == '0');
+  want_coop = !x && coop_wanted(a, d, (long long)a->B * (a->Hkv / hh) * a->splits, pdl);
+  cudaError_t e = plan_launch(a, sh, L, !sh.paged && !want_coop && !bal_wanted);
+  if (e != cudaSuccess || !bal_wanted) return e;
+  const long long slots = (long long)L.occupancy * sm_count();
+  if ((long long)a->B * L.p.hg > slots) return cudaSuccess;
+  L.p.bal_gran = (sh.paged && sh.bt > L.p.tb) ? sh.bt : L.p.tb;
+  L.blocks = (int)std::min<long long>(slots, L.blocks);
+  want_coop = !x && coop_wanted(a, d, L.blocks, pdl);
+  return cudaSuccess;
 }
 
 cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, const kvf_exchange *x = nullptr,
@@ -592,11 +639,9 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   if (e != cudaSuccess) return e;
   if (a->B == 0) return cudaSuccess;
   if (kernel == 2) return launch_tc(a, sh, stream, x, pdl);
-  // The in-launch merge needs the general kernel; contiguous caches without
-  // it run the lean one.
-  const bool want_coop = !x && coop_wanted(a, d, heads_per_block(a->Hkv, fmt, d), pdl);
   Launch L;
-  e = plan_launch(a, sh, L, !sh.paged && !want_coop);
+  bool want_coop = false;
+  e = plan_mma(a, sh, d, pdl, x, L, want_coop);
   if (e != cudaSuccess) return e;
   CUtensorMap tk, tv, tkm, tvm;
   e = encode_maps(a, sh, L.p, tk, tv);
@@ -618,7 +663,9 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   void *params[6] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv, &tkm, &tvm};
   e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl, L.p.coop_merge != 0);
   if (e != cudaSuccess) return e;
-  if (!L.p.final_out && !L.p.coop_merge) e = launch_merge(a, d, stream, true, x);
+  if (!L.p.final_out && !L.p.coop_merge)
+    e = launch_merge(a, d, stream, true, x,
+                     L.p.bal_gran > 0 ? MergeBalance{L.p.hg, L.blocks, L.p.bal_gran} : MergeBalance{0, 0, 0});
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -736,17 +783,22 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
     }
     return cudaSuccess;
   }
-  const bool want_coop = coop_wanted(a, d, heads_per_block(a->Hkv, fmt, d), false);
   Launch L;
-  e = plan_launch(a, sh, L, !sh.paged && !want_coop);
+  bool want_coop = false;
+  e = plan_mma(a, sh, d, false, nullptr, L, want_coop);
   if (e != cudaSuccess) return e;
   if (buf && buf_len > 0) {
     const KernelInfo ki = info_for(L.fn);
+    char chunk[48];
+    if (L.p.bal_gran > 0)
+      std::snprintf(chunk, sizeof(chunk), "balanced(gran=%d)", L.p.bal_gran);
+    else
+      std::snprintf(chunk, sizeof(chunk), "%d", L.p.chunk);
     std::snprintf(buf, (size_t)buf_len,
                   "kernel=mma.sync grid=%d block=%d heads/block=%d tokens/stage=%d stages=%d stage_bytes=%u "
-                  "smem=%u chunk=%d splits=%d blocks/sm=%d regs=%d final=%d meta=%s merge=%s",
+                  "smem=%u chunk=%s splits=%d blocks/sm=%d regs=%d final=%d meta=%s merge=%s",
                   L.blocks, L.threads, L.p.hh, L.p.tb, L.p.stages, L.p.stage_bytes, L.p.smem_total,
-                  L.p.chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out,
+                  chunk, L.p.splits, L.occupancy, ki.regs, L.p.final_out,
                   sh.gpr == 0 ? "none" : L.p.meta_tma ? "tma" : "cp.async",
                   L.p.final_out ? "none"
                   : want_coop && coop_fits(L.fn, L.blocks, L.threads, L.p.smem_total) ? "in-kernel(grid)" : "kernel");
@@ -759,17 +811,14 @@ extern "C" cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int 
   return kvf_b200_describe_path(a, fmt, d, ord, paged, KVF_PATH_AUTO, buf, buf_len);
 }
 
-extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group,
-                                       int paged, int block_tokens) {
+namespace kvfb {
+namespace {
+
+int suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group, int paged, int block_tokens,
+                   bool ragged) {
   if (B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || n <= 0 || (d != 64 && d != 128) || fmt < 0 || fmt > 2)
     return 1;
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
-  }
-  cudaGetLastError();
+  const int sms = sm_count();
   Shape shq;
   shq.fmt = fmt;
   shq.d = d;
@@ -833,7 +882,49 @@ extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, in
       best = s;
     }
   }
+  if (ragged && !tc && units <= slots && best > 1) {
+    // Balanced launches (plan_mma) choose the chunk themselves; the split
+    // count is the workspace's capacity per sequence. One sequence may use
+    // up to slots / head-groups splits (when the others are short); the
+    // capacity allows that while the partials stay within 64 MiB.
+    const int per = slots / (Hkv / hh);
+    const long long per_split = (long long)B * H * (d + 2) * 4;
+    const int by_bytes = (int)std::min<long long>(1024, (64ll << 20) / per_split);
+    return std::max(best, std::min({per, smax, by_bytes}));
+  }
   return best;
+}
+
+} // namespace
+} // namespace kvfb
+
+extern "C" int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group,
+                                       int paged, int block_tokens) {
+  return suggest_splits(B, H, Hkv, n, fmt, d, group, paged, block_tokens, false);
+}
+
+extern "C" int kvf_b200_balanced_chunk(const int *seq_lens, int B, int n, int splits, int units, int grid,
+                                       int gran) {
+  if (!seq_lens || B <= 0 || n < 0 || splits < 1 || units < 1 || gran < 1 || grid < 1 ||
+      (long long)units * B > grid)
+    return -1;
+  auto len_of = [&](int b) { return std::min(std::max(seq_lens[b], 0), n); };
+  long long T = 0;
+  int nz = 0;
+  for (int b = 0; b < B; ++b) {
+    T += len_of(b);
+    nz += len_of(b) > 0;
+  }
+  return balance_search(T, nz, n, splits, grid / units, gran, [&](int c) {
+    long long cnt = 0;
+    for (int b = 0; b < B; ++b) cnt += (len_of(b) + c - 1) / c;
+    return cnt;
+  });
+}
+
+extern "C" int kvf_b200_suggest_splits_ragged(int B, int H, int Hkv, int n, int fmt, int d, int group,
+                                              int paged, int block_tokens) {
+  return suggest_splits(B, H, Hkv, n, fmt, d, group, paged, block_tokens, true);
 }
 
 extern "C" unsigned kvf_b200_device_errors(void) {

@@ -77,6 +77,7 @@ struct Plan {
   int bt_shift;    // log2(tokens per page)
   int final_out;   // 1: write normalised out; 0: write partials
   int coop_merge;  // cooperative launch: the blocks merge the splits after a grid barrier
+  int bal_gran;    // > 0: token-balanced splits (see balanced_chunk), chunk granularity
   uint32_t swz;    // swizzle mask for the K/V tiles (0x70, 0x30, 0x10)
   uint32_t box_bytes;   // one TMA box
   uint32_t kv_bytes;    // K (or V) bytes in one stage
@@ -97,6 +98,102 @@ enum : unsigned { KVFB_ERR_TIMEOUT = 1u, KVFB_ERR_EXCHANGE = 2u };
 
 // (scale, zero) of an fp16 half2 metadata word.
 __device__ __forceinline__ float2 meta_sz(uint32_t w) { return ptx::unpack_f16x2(w); }
+
+// ---------------------------------------------------------------------------
+// Token-balanced splits for a batch of unequal sequences (seq_lens given).
+//
+// With one split count for every sequence, the blocks of the longest sequence
+// set the launch time while the short sequences' blocks finish early or have
+// nothing to do. Balanced, the launch has `grid` blocks for `units` head
+// groups per sequence, and all sequences share one chunk c: the smallest
+// multiple of `gran` with c >= ceil(n / S) (so no sequence needs more than
+// the workspace's S splits) for which the work items
+// units * sum_b ceil(len_b / c) fit in the grid. Sequence b then has
+// s_b = ceil(len_b / c) splits, its partials in split slots [0, s_b), and
+// no block reads more than c tokens. The chunk depends on seq_lens only, so
+// the decode blocks and the merge compute it on the device and agree, and
+// the host never reads the lengths.
+
+// The chunk search, shared by the device (warp-parallel counts) and the host
+// (plain loops): T tokens in nz non-empty sequences, per = grid / units items
+// per head group, count(c) = sum_b ceil(len_b / c), non-increasing in c.
+template <class Count>
+__host__ __device__ __forceinline__ int balance_search(long long T, int nz, int n, int S, int per, int gran,
+                                                       Count count) {
+  const long long g = gran;
+  auto up = [g](long long x) { return (x + g - 1) / g * g; };
+  const long long by_s = (n + S - 1) / S, by_t = (T + per - 1) / per;
+  long long lo = up(by_s > by_t ? by_s : by_t);
+  if (lo < g) lo = g;
+  // count(c) <= T / c + nz, so c >= T / (per - nz) is enough; a chunk of n
+  // (one split per sequence, nz <= per items) always is.
+  const long long whole = up(n > 1 ? n : 1);
+  long long hi = per > nz ? up((T + (per - nz) - 1) / (per - nz)) : whole;
+  if (hi > whole) hi = whole;
+  if (hi < lo) hi = lo;
+  while (lo < hi) {
+    const long long mid = lo + (hi - lo) / g / 2 * g;
+    if (count((int)mid) <= per) hi = mid;
+    else lo = mid + g;
+  }
+  return (int)lo;
+}
+
+__device__ __forceinline__ int seq_len_of(const kvf_args &a, int b) {
+  return min(max(__ldg(a.seq_lens + b), 0), a.n);
+}
+
+// The balanced chunk; every lane of the calling warp takes part and gets it.
+__device__ __forceinline__ int balanced_chunk(const kvf_args &a, int units, int grid, int gran) {
+  const int lane = threadIdx.x & 31;
+  long long T = 0;
+  int nz = 0;
+  for (int b0 = 0; b0 < a.B; b0 += 32) {
+    const int len = b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
+    T += len;
+    nz += len > 0;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) T += __shfl_xor_sync(0xffffffffu, T, off);
+  nz = __reduce_add_sync(0xffffffffu, (unsigned)nz);
+  return balance_search(T, nz, a.n, a.splits, grid / units, gran, [&](int c) {
+    unsigned cnt = 0;
+    for (int b0 = 0; b0 < a.B; b0 += 32) {
+      const int len = b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
+      cnt += (unsigned)((len + c - 1) / c);
+    }
+    return (long long)__reduce_add_sync(0xffffffffu, cnt);
+  });
+}
+
+// (sequence b, split) of work item j (items ordered by sequence, then split)
+// under chunk c; b = -1 when j is past the last item. Warp-collective.
+__device__ __forceinline__ void balanced_item(const kvf_args &a, int c, int j, int &b, int &split) {
+  const int lane = threadIdx.x & 31;
+  b = -1;
+  split = 0;
+  int carry = 0;
+  for (int b0 = 0; b0 < a.B; b0 += 32) {
+    const int len = b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
+    const int s = (len + c - 1) / c;
+    int incl = s;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    incl += carry;
+    const unsigned hit = __ballot_sync(0xffffffffu, incl > j);
+    if (hit) {
+      const int f = __ffs(hit) - 1;
+      const int excl = __shfl_sync(0xffffffffu, incl - s, f);
+      b = b0 + f;
+      split = j - excl;
+      return;
+    }
+    carry = __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
 
 // Integer codes go to the tensor cores centred: int8 code - 128 in [-128, 127],
 // int4 code - 8 in [-8, 7], exact in fp16. The dequantised value is then
@@ -231,23 +328,26 @@ struct MergeSmem {
 };
 
 __device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long head, int col, bool colok,
-                                             MergeSmem &sm, float &Mt, float &Lt, float &Ot, int nw = kMergeWarps) {
+                                             MergeSmem &sm, float &Mt, float &Lt, float &Ot, int nw = kMergeWarps,
+                                             int nsp = -1) {
   // kMergeWarps partial states, each over splits w, w + kMergeWarps, ...;
   // warp i of the nw warps computes states i, i + nw, ..., so the arithmetic
-  // (and the result, bit for bit) is the same for any nw.
+  // (and the result, bit for bit) is the same for any nw. Only split slots
+  // [0, nsp) hold partials (all S of them when nsp < 0).
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int S = a.splits;
+  const int NS = nsp < 0 ? S : min(nsp, S);
   const float *ml = a.part_ml + head * S * 2;
   const float *po = a.part_o + head * (long long)S * d;
 
   for (int vw = warp; vw < kMergeWarps; vw += nw) {
     float M = -INFINITY, L = 0.f, O = 0.f;
-    for (int base = vw; base < S; base += kMergeWarps * kMergeUnroll) {
+    for (int base = vw; base < NS; base += kMergeWarps * kMergeUnroll) {
       float ms[kMergeUnroll], ls[kMergeUnroll], os[kMergeUnroll];
 #pragma unroll
       for (int k = 0; k < kMergeUnroll; ++k) {
         const int sp = base + k * kMergeWarps;
-        const bool v = sp < S;
+        const bool v = sp < NS;
         ms[k] = v ? __ldcg(ml + 2 * sp) : -INFINITY;
         ls[k] = v ? __ldcg(ml + 2 * sp + 1) : 0.f;
         os[k] = (v && colok) ? __ldcg(po + (long long)sp * d + col) : 0.f;
@@ -327,15 +427,35 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   const int lane = threadIdx.x & 31;
 
   // Work item: (sequence b, head group hgi, split), split fastest so that a
-  // sequence's blocks run together.
-  const int split = blockIdx.x % p.splits;
-  const int rest = blockIdx.x / p.splits;
-  const int hgi = rest % p.hg;
-  const int b = rest / p.hg;
+  // sequence's blocks run together; balanced, head group fastest over the
+  // items of balanced_item, and a block past the last item (idle) reads and
+  // writes nothing.
+  // The epilogue reads a balanced item back from s_item (sequence or -1,
+  // split, chunk) rather than holding it in registers through the stages.
+  __shared__ int s_item[3];
+  int split, hgi, b, chunk = p.chunk;
+  bool idle = false;
+  if (!LEAN && p.bal_gran > 0) {
+    chunk = balanced_chunk(a, p.hg, gridDim.x, p.bal_gran);
+    hgi = blockIdx.x % p.hg;
+    balanced_item(a, chunk, blockIdx.x / p.hg, b, split);
+    idle = b < 0;
+    if (threadIdx.x == 0) {
+      s_item[0] = b;
+      s_item[1] = split;
+      s_item[2] = chunk;
+    }
+    if (idle) b = 0;
+  } else {
+    split = blockIdx.x % p.splits;
+    const int rest = blockIdx.x / p.splits;
+    hgi = rest % p.hg;
+    b = rest / p.hg;
+  }
   int nb = a.n;
   if (a.seq_lens) nb = min(max(a.seq_lens[b], 0), a.n);
-  const int t0 = split * p.chunk;
-  const int t1 = min(nb, t0 + p.chunk);
+  const int t0 = idle ? 0 : split * chunk;
+  const int t1 = idle ? 0 : min(nb, t0 + chunk);
   const int tbs = p.tbox_shift;
 
   __shared__ int s_abort;
@@ -969,12 +1089,20 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     }
   }
   const float finv = exp2i(max(min(-ev_run, 127), -126));
+  int eb, esplit;
+  if (!LEAN && p.bal_gran > 0) {
+    eb = s_item[0];
+    esplit = s_item[1];
+  } else {
+    esplit = blockIdx.x % p.splits;
+    eb = blockIdx.x / p.splits / p.hg;
+  }
   // O = (O_hi + O_lo) * 2^-ev + zero term; one query head per (n-tile, c4).
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int hq = nt * 4 + c4;
-    if (ok && hq < p.gq) {
-      const long long head = (long long)b * a.H + (long long)h * p.gq + hq;
+    if (ok && eb >= 0 && hq < p.gq) {
+      const long long head = (long long)eb * a.H + (long long)h * p.gq + hq;
       const float L = l_run[nt];
       const float inv = L > 0.f ? 1.f / L : 0.f;
       float *dst;
@@ -982,10 +1110,10 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
         dst = a.out + head * D;
         if (g8 == 0 && a.lse) a.lse[head] = L > 0.f ? m_run[nt] + log2f(L) : -INFINITY;
       } else {
-        dst = a.part_o + (head * p.splits + split) * D;
+        dst = a.part_o + (head * p.splits + esplit) * D;
         if (g8 == 0) {
-          a.part_ml[(head * p.splits + split) * 2] = m_run[nt];
-          a.part_ml[(head * p.splits + split) * 2 + 1] = L;
+          a.part_ml[(head * p.splits + esplit) * 2] = m_run[nt];
+          a.part_ml[(head * p.splits + esplit) * 2 + 1] = L;
         }
       }
 #pragma unroll
@@ -1048,7 +1176,8 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       const int col = zc * 32 + lane;
       const bool colok = col < D;
       float Mt, Lt, Ot;
-      merge_splits(a, D, head, col, colok, msm, Mt, Lt, Ot, p.hh);
+      const int nsp = p.bal_gran > 0 ? (seq_len_of(a, (int)(head / a.H)) + s_item[2] - 1) / s_item[2] : p.splits;
+      merge_splits(a, D, head, col, colok, msm, Mt, Lt, Ot, p.hh, nsp);
       if (warp == 0) {
         if (colok) a.out[head * D + col] = Lt > 0.f ? Ot / Lt : 0.f;
         if (lane == 0 && zc == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
@@ -1059,7 +1188,19 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   }
 }
 
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args a, int d) {
+// bal: the decode's (units, grid, gran) when its splits were token-balanced
+// (units = 0 otherwise); the split count of the sequence is then worked out
+// from seq_lens before waiting for the decode grid.
+struct MergeBalance {
+  int units, grid, gran;
+};
+
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args a, int d, const MergeBalance bal) {
+  int nsp = -1;
+  if (bal.units > 0) {
+    const int c = balanced_chunk(a, bal.units, bal.grid, bal.gran);
+    nsp = (seq_len_of(a, blockIdx.y) + c - 1) / c;
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ MergeSmem sm;
   const long long head = (long long)blockIdx.y * a.H + blockIdx.x;
@@ -1067,7 +1208,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args 
   const int col = blockIdx.z * 32 + lane;
   const bool colok = col < d;
   float Mt, Lt, Ot;
-  merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot);
+  merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot, kMergeWarps, nsp);
   if ((threadIdx.x >> 5) == 0) {
     if (colok) a.out[head * d + col] = Lt > 0.f ? Ot / Lt : 0.f;
     if (lane == 0 && blockIdx.z == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;

@@ -10,7 +10,7 @@ and predicted time), and fits the cost model's constants
     python -m kvforge_b200.sweep calibrate sweep.csv \\
         --cal kvforge_b200/machines/b200-sxm.cal                 # anywhere
 
-Timing is bench.py's: the L2 is flushed (a 3 x L2 write) before every step,
+Timing is bench.py's: the L2 is flushed (kvforge_b200.l2flush) before every step,
 each step is bracketed by CUDA events on the launching stream, and the median
 of the repetitions is kept. Inputs are the benchmark workloads' seeded
 synthetic data with the swept batch and length.
@@ -30,6 +30,7 @@ import numpy as np
 
 from . import costmodel
 from .codegen import variant_id
+from .l2flush import L2Flush
 
 FIELDS = ["name", "B", "H", "Hkv", "d", "n", "fmt", "group", "order", "paged", "block_tokens", "tokens",
           "splits", "path", "variant", "payload_bytes", "us", "us_min", "predicted_us", "suggested"]
@@ -54,12 +55,12 @@ def _time_steps(step, flush, stream, warmup: int, reps: int) -> List[float]:
     import torch
 
     for i in range(warmup):
-        flush.fill_(i & 0xFF)
+        flush(i)
         step()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
     for i, (e0, e1) in enumerate(ev):
-        flush.fill_((i + 7) & 0xFF)
+        flush(i + 7)
         e0.record(stream)
         step()
         e1.record(stream)
@@ -79,8 +80,7 @@ def run(out: Path, quick: bool = False, reps: int = 15, warmup: int = 3, max_spl
     L = lib()
     stream = torch.cuda.current_stream(dev)
     sptr = ctypes.c_void_p(stream.cuda_stream)
-    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    flush = torch.empty(max(96 << 20, 3 * l2), dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     default_model = costmodel.CostModel.load()
     rows: List[dict] = []
     for name, base, B, n in GRID:

@@ -30,6 +30,7 @@ class Workload:
     group: int
     place: Placement
     ragged: Optional[tuple] = None   # (lo, hi): n_b ~ U[lo, hi], seeded
+    lens: Optional[tuple] = None     # explicit tokens per sequence
     outlier_frac: float = 0.0        # fraction of (KV head, channel) pairs scaled x8
     q_fp16: bool = False             # queries rounded to fp16 values
     shard: str = "replicas"          # "replicas", "splitkv" or "kvheads" across GPUs
@@ -40,6 +41,8 @@ class Workload:
         return {FMT_F16: "f16", FMT_INT8: f"int8:{self.group}", FMT_INT4: f"int4:{self.group}"}[self.fmt]
 
     def seq_lens(self) -> Optional[np.ndarray]:
+        if self.lens is not None:
+            return np.asarray(self.lens, dtype=np.int32)
         if self.ragged is None:
             return None
         lo, hi = self.ragged
@@ -49,7 +52,8 @@ class Workload:
     def config(self) -> dict:
         return {
             "workload": self.name, "B": self.B, "H": self.H, "Hkv": self.Hkv, "d": self.d,
-            "n": self.n if self.ragged is None else f"U[{self.ragged[0]},{self.ragged[1]}]",
+            "n": (f"U[{self.ragged[0]},{self.ragged[1]}]" if self.ragged is not None
+                  else "/".join(map(str, self.lens)) if self.lens is not None else self.n),
             "kv_format": self.fmt_name, "layout": self.place.name,
         }
 
@@ -73,6 +77,18 @@ CONFIG_ORDER = list(CONFIGS)
 # The configuration the headline metric is quoted on at one GPU.
 HEADLINE = CONFIG_ORDER[1]
 
+# Further shapes for parity tests and measurements (not benchmark configurations):
+# one long sequence among short ones, where one split count for all sequences
+# leaves most of the GPU idle.
+EXTRA = {
+    w.name: w
+    for w in [
+        Workload("skewed_gqa_b8_n32k_f16_tm_p16", 8, 32, 8, 128, 32768, FMT_F16, 0,
+                 Placement(ORD_TOKEN, True, 16), lens=(32768,) + (1024,) * 7),
+    ]
+}
+WORKLOADS = {**CONFIGS, **EXTRA}
+
 
 def generate(w: Workload, device, seed: Optional[int] = None):
     """Seeded inputs for workload w: q [B,H,D], K and V [B,Hkv,n,D] (float32,
@@ -94,4 +110,4 @@ def generate(w: Workload, device, seed: Optional[int] = None):
     return q, K, V, w.seq_lens()
 
 
-__all__ = ["Workload", "CONFIGS", "CONFIG_ORDER", "HEADLINE", "generate"]
+__all__ = ["Workload", "CONFIGS", "CONFIG_ORDER", "HEADLINE", "EXTRA", "WORKLOADS", "generate"]

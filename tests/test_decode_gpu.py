@@ -448,3 +448,87 @@ def test_in_launch_grid_merge_equals_merge_kernel(cuda, monkeypatch, B, H, Hkv, 
         assert int(ws.split_sem.abs().sum()) == 0
     assert torch.equal(outs["0"], outs["1"])
     assert api.device_errors() == 0
+
+
+@pytest.mark.parametrize("fmt,group,place", [
+    (FMT_F16, 0, Placement(ORD_TOKEN, True, 16)),
+    (FMT_INT8, 64, Placement(ORD_HEAD, False, 0)),
+], ids=["f16_tm_p16", "int8_hm"])
+def test_balanced_splits_on_ragged_batches(cuda, monkeypatch, fmt, group, place):
+    """Sequences of unequal length share one chunk of tokens (the mma.sync
+    launch balances them over one wave of blocks): the device picks the chunk
+    kvf_b200_balanced_chunk computes on the host (each sequence's partials
+    fill exactly its first ceil(len / chunk) split slots), the output matches
+    the oracle, and the cooperative in-launch merge, the merge kernel and a
+    zero-copy Decoder step (merge kernel after a dependent launch) agree bit
+    for bit."""
+    monkeypatch.setenv("KVF_B200_TC", "0")
+    rs = np.random.RandomState(43)
+    B, H, Hkv, D, n = 8, 32, 8, 128, 2048
+    lens = np.array([2048, 0, 1, 700, 1999, 64, 1500, 333], dtype=np.int32)
+    q = rs.standard_normal((B, H, D)).astype(np.float32)
+    K = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
+    V = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
+    _, _, kd = O.quantize(fmt, D, group, K.reshape(-1, D))
+    _, _, vd = O.quantize(fmt, D, group, V.reshape(-1, D))
+    ref = O.attention(q, kd.reshape(K.shape), vd.reshape(V.shape), O.scale_f32(D), seq_lens=lens)
+    qd = torch.as_tensor(q, device=cuda)
+    cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                     fmt=fmt, group=group, place=place, seq_lens=lens)
+    S = api.suggest_splits(cache, H)
+    bt = place.block_tokens if place.paged else 0
+    assert S >= lib().kvf_b200_suggest_splits(B, H, Hkv, n, fmt, D, group, int(place.paged), bt)
+    ws = api.Workspace.allocate(B, H, D, S, cuda)
+    desc = api.describe(qd, cache, ws, path="mma")
+    assert "chunk=balanced" in desc, desc
+    f = dict(kv.split("=", 1) for kv in desc.split() if "=" in kv)
+    grid, hh = int(f["grid"]), int(f["heads/block"])
+    gran = int(f["chunk"].split("gran=")[1].rstrip(")"))
+    c = int(lib().kvf_b200_balanced_chunk(lens.ctypes.data_as(ctypes.c_void_p), B, n, S, Hkv // hh, grid, gran))
+    assert c > 0
+    sb = (lens.astype(np.int64) + c - 1) // c
+    outs = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("KVF_B200_COOP", mode)
+        ws.part_ml.fill_(float("nan"))
+        outs[mode] = api.decode(qd, cache, workspace=ws, path="mma").clone()
+        torch.cuda.synchronize()
+        written = torch.isfinite(ws.part_ml[..., 0]).cpu().numpy()  # [B][H][S]
+        want = np.arange(S)[None, None, :] < sb[:, None, None]
+        assert np.array_equal(written, np.broadcast_to(want, written.shape)), mode
+        assert_close(outs[mode].cpu().numpy(), ref, f"coop={mode}")
+        assert int(ws.split_sem.abs().sum()) == 0
+    assert torch.equal(outs["0"], outs["1"])
+    assert np.all(outs["0"][1].cpu().numpy() == 0.0)
+    monkeypatch.delenv("KVF_B200_COOP")
+    dec = api.Decoder(cache, H, splits=S, path="mma")
+    got = dec.step(torch.as_tensor(q))
+    assert torch.equal(got, outs["1"].cpu())
+    # KVF_B200_BALANCE=0: one split count for all sequences, same results.
+    monkeypatch.setenv("KVF_B200_BALANCE", "0")
+    assert "chunk=balanced" not in api.describe(qd, cache, ws, path="mma")
+    uni = api.decode(qd, cache, workspace=ws, path="mma").cpu().numpy()
+    assert_close(uni, ref, "unbalanced")
+    assert np.abs(uni - outs["1"].cpu().numpy()).max() < 1e-5
+    assert api.device_errors() == 0
+
+
+def test_balanced_splits_fall_back_when_units_exceed_one_wave(cuda, monkeypatch):
+    """More (sequence, head group) units than one wave of blocks: the launch
+    keeps the uniform split plan, with the same results."""
+    monkeypatch.setenv("KVF_B200_TC", "0")
+    rs = np.random.RandomState(44)
+    B, H, Hkv, D, n = 320, 4, 4, 64, 40
+    lens = rs.randint(0, n + 1, size=B).astype(np.int32)
+    q = rs.standard_normal((B, H, D)).astype(np.float32)
+    K = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
+    V = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
+    ref = O.attention(q, O.h2f(O.f2h(K)), O.h2f(O.f2h(V)), O.scale_f32(D), seq_lens=lens)
+    qd = torch.as_tensor(q, device=cuda)
+    cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                     fmt=FMT_F16, place=Placement(ORD_HEAD, False, 0), seq_lens=lens)
+    ws = api.Workspace.allocate(B, H, D, 3, cuda)
+    desc = api.describe(qd, cache, ws)
+    assert "chunk=balanced" not in desc, desc
+    assert_close(api.decode(qd, cache, workspace=ws).cpu().numpy(), ref, "uniform plan")
+    assert api.device_errors() == 0
