@@ -339,11 +339,49 @@ cudaError_t encode_maps_box(const kvf_args *a, const Shape &sh, int rbytes, int 
   return cudaSuccess;
 }
 
+// Streaming multiprocessors of the current device (148 when it cannot be asked).
+int sm_count() {
+  static std::atomic<int> cache[16];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (dev >= 0 && dev < 16) {
+    const int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+    cudaGetLastError();
+    v = 148;
+  }
+  if (dev >= 0 && dev < 16) cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+// Blocks of merge_kernel resident per SM (at least 1).
+int merge_blocks_per_sm() {
+  static std::atomic<int> v{0};
+  int r = v.load(std::memory_order_relaxed);
+  if (r > 0) return r;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, merge_kernel, kMergeWarps * 32, 0) != cudaSuccess || r < 1) {
+    cudaGetLastError();
+    r = 1;
+  }
+  v.store(r, std::memory_order_relaxed);
+  return r;
+}
+
 cudaError_t launch_merge(const kvf_args *a, int d, cudaStream_t st, bool pdl, const kvf_exchange *x = nullptr,
                          MergeBalance bal = MergeBalance{0, 0, 0}) {
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3((unsigned)a->H, (unsigned)a->B, (unsigned)((d + 31) / 32));
+  const long long slices = (long long)a->H * a->B * ((d + 31) / 32);
+  if (x)
+    cfg.gridDim = dim3((unsigned)a->H, (unsigned)a->B, (unsigned)((d + 31) / 32));
+  else
+    cfg.gridDim = dim3((unsigned)std::min<long long>(slices, (long long)sm_count() * merge_blocks_per_sm()), 1, 1);
   cfg.blockDim = dim3(kMergeWarps * 32, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
@@ -554,26 +592,6 @@ bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
   return blocks <= per_sm * sms;
 }
 
-// Streaming multiprocessors of the current device (148 when it cannot be asked).
-int sm_count() {
-  static std::atomic<int> cache[16];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return 148;
-  }
-  if (dev >= 0 && dev < 16) {
-    const int v = cache[dev].load(std::memory_order_relaxed);
-    if (v > 0) return v;
-  }
-  int v = 0;
-  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
-    cudaGetLastError();
-    v = 148;
-  }
-  if (dev >= 0 && dev < 16) cache[dev].store(v, std::memory_order_relaxed);
-  return v;
-}
 
 // The mma.sync launch: plan, token-balanced splits, in-launch merge.
 //
@@ -882,7 +900,8 @@ int suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group, int 
       best = s;
     }
   }
-  if (ragged && !tc && units <= slots && best > 1) {
+  const char *env = std::getenv("KVF_B200_BALANCE");
+  if (ragged && !tc && units <= slots && best > 1 && !(env && env[0] == '0')) {
     // Balanced launches (plan_mma) choose the chunk themselves; the split
     // count is the workspace's capacity per sequence. One sequence may use
     // up to slots / head-groups splits (when the others are short); the

@@ -130,7 +130,8 @@ __host__ __device__ __forceinline__ int balance_search(long long T, int nz, int 
   const long long whole = up(n > 1 ? n : 1);
   long long hi = per > nz ? up((T + (per - nz) - 1) / (per - nz)) : whole;
   if (hi > whole) hi = whole;
-  if (hi < lo) hi = lo;
+  if (hi <= lo || count((int)lo) <= per) return (int)lo;  // the usual case: the lower bound fits
+  lo += g;
   while (lo < hi) {
     const long long mid = lo + (hi - lo) / g / 2 * g;
     if (count((int)mid) <= per) hi = mid;
@@ -143,13 +144,20 @@ __device__ __forceinline__ int seq_len_of(const kvf_args &a, int b) {
   return min(max(__ldg(a.seq_lens + b), 0), a.n);
 }
 
+// Lane i's first length, seq_lens[i] (0 past the batch): kept in a register
+// so that batches of up to 32 sequences read seq_lens once.
+__device__ __forceinline__ int first_len(const kvf_args &a) {
+  const int lane = threadIdx.x & 31;
+  return lane < a.B ? seq_len_of(a, lane) : 0;
+}
+
 // The balanced chunk; every lane of the calling warp takes part and gets it.
-__device__ __forceinline__ int balanced_chunk(const kvf_args &a, int units, int grid, int gran) {
+__device__ __forceinline__ int balanced_chunk(const kvf_args &a, int len0, int units, int grid, int gran) {
   const int lane = threadIdx.x & 31;
   long long T = 0;
   int nz = 0;
   for (int b0 = 0; b0 < a.B; b0 += 32) {
-    const int len = b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
+    const int len = b0 == 0 ? len0 : b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
     T += len;
     nz += len > 0;
   }
@@ -159,7 +167,7 @@ __device__ __forceinline__ int balanced_chunk(const kvf_args &a, int units, int 
   return balance_search(T, nz, a.n, a.splits, grid / units, gran, [&](int c) {
     unsigned cnt = 0;
     for (int b0 = 0; b0 < a.B; b0 += 32) {
-      const int len = b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
+      const int len = b0 == 0 ? len0 : b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
       cnt += (unsigned)((len + c - 1) / c);
     }
     return (long long)__reduce_add_sync(0xffffffffu, cnt);
@@ -168,13 +176,13 @@ __device__ __forceinline__ int balanced_chunk(const kvf_args &a, int units, int 
 
 // (sequence b, split) of work item j (items ordered by sequence, then split)
 // under chunk c; b = -1 when j is past the last item. Warp-collective.
-__device__ __forceinline__ void balanced_item(const kvf_args &a, int c, int j, int &b, int &split) {
+__device__ __forceinline__ void balanced_item(const kvf_args &a, int len0, int c, int j, int &b, int &split) {
   const int lane = threadIdx.x & 31;
   b = -1;
   split = 0;
   int carry = 0;
   for (int b0 = 0; b0 < a.B; b0 += 32) {
-    const int len = b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
+    const int len = b0 == 0 ? len0 : b0 + lane < a.B ? seq_len_of(a, b0 + lane) : 0;
     const int s = (len + c - 1) / c;
     int incl = s;
 #pragma unroll
@@ -436,9 +444,10 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
   int split, hgi, b, chunk = p.chunk;
   bool idle = false;
   if (!LEAN && p.bal_gran > 0) {
-    chunk = balanced_chunk(a, p.hg, gridDim.x, p.bal_gran);
+    const int len0 = first_len(a);
+    chunk = balanced_chunk(a, len0, p.hg, gridDim.x, p.bal_gran);
     hgi = blockIdx.x % p.hg;
-    balanced_item(a, chunk, blockIdx.x / p.hg, b, split);
+    balanced_item(a, len0, chunk, blockIdx.x / p.hg, b, split);
     idle = b < 0;
     if (threadIdx.x == 0) {
       s_item[0] = b;
@@ -1189,29 +1198,37 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
 }
 
 // bal: the decode's (units, grid, gran) when its splits were token-balanced
-// (units = 0 otherwise); the split count of the sequence is then worked out
-// from seq_lens before waiting for the decode grid.
+// (units = 0 otherwise); each sequence's split count then follows from
+// seq_lens and the chunk, which the block works out before waiting for the
+// decode grid.
 struct MergeBalance {
   int units, grid, gran;
 };
 
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const kvf_args a, int d, const MergeBalance bal) {
-  int nsp = -1;
-  if (bal.units > 0) {
-    const int c = balanced_chunk(a, bal.units, bal.grid, bal.gran);
-    nsp = (seq_len_of(a, blockIdx.y) + c - 1) / c;
-  }
+// A persistent grid (at most one wave): block i merges the (query head,
+// 32-column) slices i, i + grid, ... in the order of the reference's
+// (head, sequence, slice) grid, so that a block pays its start-up once.
+__global__ void __launch_bounds__(kMergeWarps * 32, 2) merge_kernel(const kvf_args a, int d, const MergeBalance bal) {
+  int c = 0;
+  if (bal.units > 0) c = balanced_chunk(a, first_len(a), bal.units, bal.grid, bal.gran);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ MergeSmem sm;
-  const long long head = (long long)blockIdx.y * a.H + blockIdx.x;
   const int lane = threadIdx.x & 31;
-  const int col = blockIdx.z * 32 + lane;
-  const bool colok = col < d;
-  float Mt, Lt, Ot;
-  merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot, kMergeWarps, nsp);
-  if ((threadIdx.x >> 5) == 0) {
-    if (colok) a.out[head * d + col] = Lt > 0.f ? Ot / Lt : 0.f;
-    if (lane == 0 && blockIdx.z == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
+  const int nz = (d + 31) / 32;
+  const long long items = (long long)a.B * a.H * nz;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+    const long long head = it / nz;  // sequence * H + query head
+    const int zc = (int)(it - head * nz);
+    const int col = zc * 32 + lane;
+    const bool colok = col < d;
+    const int nsp = c > 0 ? (seq_len_of(a, (int)(head / a.H)) + c - 1) / c : -1;
+    float Mt, Lt, Ot;
+    merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot, kMergeWarps, nsp);
+    if ((threadIdx.x >> 5) == 0) {
+      if (colok) a.out[head * d + col] = Lt > 0.f ? Ot / Lt : 0.f;
+      if (lane == 0 && zc == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
+    }
+    __syncthreads();  // sm is reused by the next slice
   }
 }
 
