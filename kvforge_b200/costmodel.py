@@ -88,17 +88,31 @@ def tokens_per_stage(s: Shape, path: str) -> int:
     return 16 * (1 if rb >= 256 else 2 if rb >= 128 else 4)
 
 
-def features(s: Shape, splits: int, path: str) -> np.ndarray:
-    """[1, payload MB, waves x stages per block, splits > 1, partials MB]."""
+def features(s: Shape, splits: int, path: str, balanced: bool = False) -> np.ndarray:
+    """[1, payload MB, waves x stages per block, splits > 1, partials MB].
+
+    balanced: the launch shared the tokens of unequal sequences out over one
+    wave of blocks (mma.sync with seq_lens, decode.cu plan_mma); the chunk is
+    then at least tokens / (blocks per head group), the kernels' own rule
+    without the per-sequence rounding."""
     hh = heads_per_block(s.Hkv, path)
     units = s.B * (s.Hkv // hh)
     tb = tokens_per_stage(s, path)
     gran = max(tb, s.block_tokens) if s.paged else tb
-    per = math.ceil(s.n / max(1, splits))
-    chunk = max(gran, math.ceil(per / gran) * gran)
-    stages = math.ceil(min(chunk, s.n) / tb)
-    waves = math.ceil(units * splits / (SMS * BLOCKS_PER_SM))
-    partial_mb = s.B * s.H * splits * (s.d + 2) * 4 / 1e6 if splits > 1 else 0.0
+    up = lambda x: max(gran, math.ceil(x / gran) * gran)  # noqa: E731
+    slots = SMS * BLOCKS_PER_SM
+    if balanced and path == "mma" and splits > 1 and units <= slots:
+        toks = s.tokens if s.tokens is not None else s.B * s.n
+        per_group = min(slots, units * splits) // (s.Hkv // hh)
+        chunk = up(max(math.ceil(s.n / splits), math.ceil(toks / per_group)))
+        stages = math.ceil(min(chunk, s.n) / tb)
+        waves = 1
+        partial_mb = s.H * math.ceil(toks / chunk + s.B / 2) * (s.d + 2) * 4 / 1e6
+    else:
+        chunk = up(math.ceil(s.n / max(1, splits)))
+        stages = math.ceil(min(chunk, s.n) / tb)
+        waves = math.ceil(units * splits / slots)
+        partial_mb = s.B * s.H * splits * (s.d + 2) * 4 / 1e6 if splits > 1 else 0.0
     return np.array([1.0, s.payload_bytes() / 1e6, float(waves * stages), 1.0 if splits > 1 else 0.0, partial_mb])
 
 
@@ -144,9 +158,9 @@ class CostModel:
                 coef[p][k] = float(val)
         return cls(coef, str(path))
 
-    def predict_us(self, s: Shape, splits: int, path: str) -> float:
+    def predict_us(self, s: Shape, splits: int, path: str, balanced: bool = False) -> float:
         c = self.coef[path]
-        return float(np.dot(features(s, splits, path), [c[k] for k in KEYS]))
+        return float(np.dot(features(s, splits, path, balanced), [c[k] for k in KEYS]))
 
     def save(self, path: Path, header: Sequence[str] = ()) -> None:
         lines = ["# kvforge_b200 cost-model constants (B200, sm_100a), fitted by kvforge_b200.sweep."]
@@ -169,7 +183,7 @@ def fit(rows: Iterable[dict]) -> CostModel:
         by_path.setdefault(r["path"], []).append(r)
     coef = {p: dict(v) for p, v in DEFAULTS.items()}
     for p, rs in by_path.items():
-        A = np.stack([features(_shape(r), int(r["splits"]), p) for r in rs])
+        A = np.stack([features(_shape(r), int(r["splits"]), p, _balanced(r)) for r in rs])
         y = np.array([float(r["us"]) for r in rs])
         w = 1.0 / y
         x, _ = nnls(A * w[:, None], y * w)
@@ -183,8 +197,13 @@ def _shape(r: dict) -> Shape:
                  int(r["tokens"]) if r.get("tokens") not in (None, "", "None") else None)
 
 
+def _balanced(r: dict) -> bool:
+    """Rows of sweeps taken before launches balanced have no such column."""
+    return str(r.get("balanced") or "0") not in ("0", "False", "")
+
+
 def relative_errors(model: CostModel, rows: Iterable[dict]) -> np.ndarray:
-    return np.array([model.predict_us(_shape(r), int(r["splits"]), r["path"]) / float(r["us"]) - 1.0
+    return np.array([model.predict_us(_shape(r), int(r["splits"]), r["path"], _balanced(r)) / float(r["us"]) - 1.0
                      for r in rows])
 
 

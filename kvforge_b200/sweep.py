@@ -33,7 +33,7 @@ from .codegen import variant_id
 from .l2flush import L2Flush
 
 FIELDS = ["name", "B", "H", "Hkv", "d", "n", "fmt", "group", "order", "paged", "block_tokens", "tokens",
-          "splits", "path", "variant", "payload_bytes", "us", "us_min", "predicted_us", "suggested"]
+          "splits", "path", "variant", "payload_bytes", "us", "us_min", "predicted_us", "suggested", "balanced"]
 
 # (name, base workload, batch, tokens per sequence); None keeps the base's.
 GRID = [
@@ -119,6 +119,7 @@ def run(out: Path, quick: bool = False, reps: int = 15, warmup: int = 3, max_spl
                           L.kvf_b200_decode_path(ctypes.byref(a), w.fmt, w.d, g, w.place.order, int(w.place.paged),
                                                  code, sptr))
 
+                balanced = "chunk=balanced" in api.describe(q, cache, ws, path=path)
                 ts = _time_steps(step, flush, stream, warmup, reps if shape.payload_bytes() < 1e9 else max(5, reps // 3))
                 errs = api.device_errors()
                 if errs:
@@ -132,8 +133,8 @@ def run(out: Path, quick: bool = False, reps: int = 15, warmup: int = 3, max_spl
                     "variant": variant_id(w.fmt, w.place.order, w.place.paged, g, 2, w.d, path),
                     "payload_bytes": shape.payload_bytes(), "us": round(float(np.median(ts)), 3),
                     "us_min": round(float(np.min(ts)), 3),
-                    "predicted_us": round(default_model.predict_us(shape, s, path), 3),
-                    "suggested": int(s == suggested),
+                    "predicted_us": round(default_model.predict_us(shape, s, path, balanced), 3),
+                    "suggested": int(s == suggested), "balanced": int(balanced),
                 })
                 print(f"{name:30s} {path:3s} splits={s:4d} {rows[-1]['us']:9.2f} us", flush=True)
                 del ws
@@ -167,7 +168,8 @@ def planner_report(model: costmodel.CostModel, rows: Sequence[dict]) -> List[dic
     rep = []
     for name, rs in by.items():
         best = min(rs, key=lambda r: float(r["us"]))
-        pick = min(rs, key=lambda r: model.predict_us(costmodel._shape(r), int(r["splits"]), r["path"]))
+        pick = min(rs, key=lambda r: model.predict_us(costmodel._shape(r), int(r["splits"]), r["path"],
+                                                        costmodel._balanced(r)))
         sugg = [r for r in rs if int(r["suggested"])]
         rep.append({"name": name, "best_us": float(best["us"]), "best": f"{best['path']}/{best['splits']}",
                     "model_us": float(pick["us"]), "model": f"{pick['path']}/{pick['splits']}",

@@ -95,3 +95,20 @@ def test_ragged_split_suggestion():
     assert rag >= uni >= 1 and rag <= 8192 // 16
     for args in [(64, 64, 8, 16384, 1, 128, 64, 1, 16), (400, 8, 4, 512, 0, 128, 0, 0, 0)]:
         assert l.kvf_b200_suggest_splits_ragged(*args) == l.kvf_b200_suggest_splits(*args), args
+
+
+def test_cost_model_follows_balanced_launches():
+    """The planner's model of a balanced launch: one wave, blocks of at least
+    tokens / (blocks per head group) tokens, partials of the used splits
+    only; unchanged for the tensor-core path and for launches that did not
+    balance (sweep rows taken before launches balanced)."""
+    from kvforge_b200 import costmodel
+
+    s = costmodel.Shape(8, 32, 8, 128, 32768, 0, 0, True, 16, 32768 + 7 * 1024)
+    bal = costmodel.features(s, 148, "mma", balanced=True)
+    uni = costmodel.features(s, 148, "mma", balanced=False)
+    assert bal[2] == 17          # 272-token chunks, 16-token stages, one wave
+    assert uni[2] == 8 * 14      # 224-token chunks, 2368 blocks in 8 waves
+    assert bal[4] < uni[4]
+    assert np.array_equal(costmodel.features(s, 4, "tc", balanced=True), costmodel.features(s, 4, "tc"))
+    assert costmodel._balanced({"balanced": "1"}) and not costmodel._balanced({})
