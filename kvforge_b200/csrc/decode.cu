@@ -559,16 +559,18 @@ cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint
 
 // Whether a decode launch should merge its splits itself (cooperative launch,
 // grid barrier): partials to merge, split counters with room for the barrier
-// words (two or more (sequence, KV head) units), no programmatic dependency
-// on a preceding kernel. It pays once the separate merge kernel is large:
+// words (two or more (sequence, KV head) units); behind a programmatic
+// dependency too (the zero-copy step's staging kernel), falling back to the
+// merge kernel where the runtime refuses that pair. It pays once the
+// separate merge kernel is large:
 // measured on B200, 8 sequences with 1024 merge slices (query head x 32
 // columns) for 288 decode blocks step in 53.7 us instead of 57.2, while
 // single sequences with 128 slices for ~295 blocks lose 1.4-2.5 us (the
 // cooperative launch costs more than the merge kernel it replaces). So by
 // default it is used from two slices per decode block; KVF_B200_COOP=1
 // forces it where possible, =0 never uses it.
-bool coop_wanted(const kvf_args *a, int d, long long blocks, bool pdl) {
-  if (a->splits <= 1 || !a->split_sem || (long long)a->B * a->Hkv < 2 || pdl) return false;
+bool coop_wanted(const kvf_args *a, int d, long long blocks) {
+  if (a->splits <= 1 || !a->split_sem || (long long)a->B * a->Hkv < 2) return false;
   const char *e = std::getenv("KVF_B200_COOP");
   if (e && e[0] == '0') return false;
   if (e && e[0] == '1') return true;
@@ -603,19 +605,18 @@ bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
 // 296 block slots busy, each block reading up to 464 tokens; balanced, 296
 // blocks read at most ~336. The in-launch merge and the balanced splits need
 // the general kernel; contiguous caches without either run the lean one.
-cudaError_t plan_mma(const kvf_args *a, const Shape &sh, int d, bool pdl, const kvf_exchange *x, Launch &L,
-                     bool &want_coop) {
+cudaError_t plan_mma(const kvf_args *a, const Shape &sh, int d, const kvf_exchange *x, Launch &L, bool &want_coop) {
   const int hh = heads_per_block(a->Hkv, sh.fmt, sh.d);
   const char *env = std::getenv("KVF_B200_BALANCE");  // 0: one split count for all sequences
   const bool bal_wanted = !x && a->seq_lens && a->splits > 1 && !(env && env[0] == '0');
-  want_coop = !x && coop_wanted(a, d, (long long)a->B * (a->Hkv / hh) * a->splits, pdl);
+  want_coop = !x && coop_wanted(a, d, (long long)a->B * (a->Hkv / hh) * a->splits);
   cudaError_t e = plan_launch(a, sh, L, !sh.paged && !want_coop && !bal_wanted);
   if (e != cudaSuccess || !bal_wanted) return e;
   const long long slots = (long long)L.occupancy * sm_count();
   if ((long long)a->B * L.p.hg > slots) return cudaSuccess;
   L.p.bal_gran = (sh.paged && sh.bt > L.p.tb) ? sh.bt : L.p.tb;
   L.blocks = (int)std::min<long long>(slots, L.blocks);
-  want_coop = !x && coop_wanted(a, d, L.blocks, pdl);
+  want_coop = !x && coop_wanted(a, d, L.blocks);
   return cudaSuccess;
 }
 
@@ -659,7 +660,7 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   if (kernel == 2) return launch_tc(a, sh, stream, x, pdl);
   Launch L;
   bool want_coop = false;
-  e = plan_mma(a, sh, d, pdl, x, L, want_coop);
+  e = plan_mma(a, sh, d, x, L, want_coop);
   if (e != cudaSuccess) return e;
   CUtensorMap tk, tv, tkm, tvm;
   e = encode_maps(a, sh, L.p, tk, tv);
@@ -677,9 +678,17 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   if (e != cudaSuccess) return e;
   L.p.coop_merge = (want_coop && !L.p.final_out && coop_fits(L.fn, L.blocks, L.threads, L.p.smem_total)) ? 1 : 0;
   const kvf_args args = *a;
-  const Plan plan = L.p;
-  void *params[6] = {const_cast<kvf_args *>(&args), const_cast<Plan *>(&plan), &tk, &tv, &tkm, &tvm};
+  Plan plan = L.p;
+  void *params[6] = {const_cast<kvf_args *>(&args), &plan, &tk, &tv, &tkm, &tvm};
   e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl, L.p.coop_merge != 0);
+  if (e != cudaSuccess && L.p.coop_merge && pdl) {
+    // Not taken as a cooperative launch behind a programmatic dependency:
+    // the merge goes to its own kernel instead.
+    cudaGetLastError();
+    L.p.coop_merge = 0;
+    plan.coop_merge = 0;
+    e = launch_params(L.fn, L.blocks, L.threads, params, L.p.smem_total, stream, pdl, false);
+  }
   if (e != cudaSuccess) return e;
   if (!L.p.final_out && !L.p.coop_merge)
     e = launch_merge(a, d, stream, true, x,
@@ -803,7 +812,7 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
   }
   Launch L;
   bool want_coop = false;
-  e = plan_mma(a, sh, d, false, nullptr, L, want_coop);
+  e = plan_mma(a, sh, d, nullptr, L, want_coop);
   if (e != cudaSuccess) return e;
   if (buf && buf_len > 0) {
     const KernelInfo ki = info_for(L.fn);
