@@ -506,7 +506,6 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
   L.occupancy = occ;
   p.stages = stages;
   p.off_q = (uint32_t)stages * p.stage_bytes;
-  p.off_p = 0;
   p.off_misc = p.off_q + ((qtile + 1023u) & ~1023u);
   p.smem_total = 1024u + p.off_misc + misc;
   uint32_t cols = (uint32_t)(2 * sh.gpr * ns + np);

@@ -72,7 +72,6 @@ struct TcPlan {
   uint32_t stage_bytes;  // K tile, V tile (128 x 128 bytes each), K meta, V meta; 1024-aligned
   uint32_t meta_bytes;   // one metadata area: 128 rows x groups x 4 bytes, 128-aligned
   uint32_t off_q;        // Q plane tile: NS rows x 128 bytes, 128-byte swizzle
-  uint32_t off_p;        // unused: the P' tile of a stage lives in its K tile
   uint32_t ptile_bytes;  // P' tile bytes (<= the K tile)
   uint32_t off_misc;     // scalars, exchange areas, barriers
   uint32_t tmem_cols;    // allocated tensor-memory columns

@@ -138,7 +138,7 @@ extern "C" cudaError_t kvf_b200_wait_merge_states(const float *gathered, const i
 }
 
 // Device buffers shared across processes of one node through CUDA IPC (plain
-// peer mappings, no multicast objects). The exporting process allocates
+// peer mappings only). The exporting process allocates
 // (zeroed) and passes the 64-byte handle to the others, which open it.
 extern "C" cudaError_t kvf_b200_ipc_alloc(size_t bytes, void **ptr, void *handle64) {
   if (!ptr || !handle64 || bytes == 0) return cudaErrorInvalidValue;
