@@ -64,6 +64,8 @@ def parse():
     p.add_argument("--batch", type=int, default=0,
                    help="override the workload's batch (smaller captures for ncu); reported in config")
     p.add_argument("--cpu-sample-s", type=float, default=15.0, help="CPU baseline budget (s)")
+    p.add_argument("--op", default="decode", choices=["decode", "quantize"],
+                   help="quantize: the device KV quantizer over the workload's K and V rows (one GPU)")
     return p.parse_args()
 
 
@@ -277,6 +279,90 @@ def cpu_baseline(w, budget_s: float) -> dict:
 METRIC = "decode-attn effective KV TB/s (payload bytes / us per step)"
 
 
+def run_quantize(args, w) -> None:
+    """The KV quantizer (kvf_b200_quantize, bit-exact with kvf::quantize,
+    runtime/kvf_host.h:72-120) over the workload's logical K and V rows: one
+    step quantizes both, with L2 flushed before it. Algorithmic bytes per
+    row: 4 * D read, row bytes + 4 * D/G written. The CPU baseline is the
+    reference's kvf::quantize (oracle/_ref, else the C restatement) on a
+    bounded sample of rows, one thread, as the reference runs it."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from kvforge_b200 import api, l2flush, workloads
+    from kvforge_b200._native import check, lib
+    from oracle import oracle as O
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    _, K, V, _ = workloads.generate(w, dev)
+    rows = K.numel() // w.d
+    rb, gpr = api.row_bytes(w.fmt, w.d), api.groups_per_row(w.fmt, w.d, w.group)
+    bufs = []
+    for X in (K, V):
+        data = torch.empty((rows, rb), dtype=torch.uint8, device=dev)
+        meta = torch.empty((rows, max(gpr, 1)), dtype=torch.int32, device=dev)
+        bufs.append((X.reshape(rows, w.d), data, meta))
+    L = lib()
+
+    def step():
+        for X, data, meta in bufs:
+            check("kvf_b200_quantize", L.kvf_b200_quantize(w.fmt, w.d, w.group, X.data_ptr(), rows, data.data_ptr(),
+                                                           meta.data_ptr() if gpr else None, sptr))
+
+    flush = l2flush.L2Flush(dev)
+    for i in range(args.warmup):
+        flush(i)
+        step()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            flush(i)
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    per_row = 4 * w.d + rb + 4 * gpr
+    algo = 2 * rows * per_row
+    gbs = algo / (ms * 1e-3) / 1e9
+    peaks = measured_peaks()
+
+    # CPU: the reference quantizer on a bounded sample of K rows.
+    sample = min(rows, 1 << 16)
+    Xs = K.reshape(rows, w.d)[:sample].cpu().numpy()
+    q = O.Ref.quantize if O.Ref.available() else O.quantize
+    q(w.fmt, w.d, w.group, Xs[:1024])
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 1 or (time.perf_counter() - t0 < min(args.cpu_sample_s, 20.0) and reps < 50):
+        q(w.fmt, w.d, w.group, Xs)
+        reps += 1
+    cpu_s = (time.perf_counter() - t0) / reps
+    cpu_gbs = sample * per_row / cpu_s / 1e9
+    line = {
+        "metric": "KV quantize throughput (algorithmic bytes / us per step)", "value": gbs, "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_step": ms * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {1: "fp32 -> int8", 2: "fp32 -> int4", 0: "fp32 -> f16"}[w.fmt], "data": "synthetic",
+        "config": {"workload": w.name, "rows_per_step": 2 * rows, "d": w.d, "group": w.group,
+                   "bytes_per_row": per_row, "l2": l2flush.DESCRIPTION},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                     "peak_source": peaks["source"] + " copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
+        "cpu_baseline": {"value": cpu_gbs, "unit": "GB/s", "cores": 1,
+                         "kind": "reference" if O.Ref.available() else "port",
+                         "sample": f"{sample} K rows, {reps} passes, kvf::quantize"},
+        "gpu_launches": 2 * args.steps, "clocks": clk.record(), "device_errors": api.device_errors(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args.gpus)
@@ -288,6 +374,11 @@ def main():
         import dataclasses
 
         w = dataclasses.replace(w, B=args.batch)
+    if args.op == "quantize":
+        if world > 1:
+            raise SystemExit("--op quantize runs on one GPU")
+        run_quantize(args, w)
+        return
     if args.impl == "reference":
         run_reference_arm(args, w, world, rank)
         if world > 1:
