@@ -67,6 +67,66 @@ __global__ void quantize_groups(const float *__restrict__ x, long long rows, int
   }
 }
 
+// Coalesced form of quantize_groups for groups of 4..D channels (powers of
+// two): lane li of a row holds channels 4 li .. 4 li + 3 (one 16-byte load),
+// a group spans group / 4 lanes, and its min and max are combined across them
+// with shuffles. The combination keeps the host loop's results bit for bit:
+// a lane that does not hold the group's first element folds its values into
+// +inf / -inf (NaNs never replace a running value in the host loop, which
+// starts from the first element), the first lane starts from that element
+// (a NaN there stays NaN), and two adjacent ranges combine as the loop
+// would have met them, earlier range first (ties keep the earlier value).
+template <int FMT, int D>
+__global__ void __launch_bounds__(256) quantize_rows(const float *__restrict__ x, long long rows, int group,
+                                                     uint8_t *__restrict__ data, uint32_t *__restrict__ meta) {
+  constexpr int LPR = D / 4;     // lanes per row
+  constexpr int RPW = 32 / LPR;  // rows per warp
+  const int lane = threadIdx.x & 31;
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long r = wid * RPW + lane / LPR;
+  const int li = lane % LPR;
+  const bool valid = r < rows;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (valid) v = __ldcs(reinterpret_cast<const float4 *>(x + r * D) + li);
+  const int lpg = group >> 2;  // lanes per group
+  const bool first = (li & (lpg - 1)) == 0;
+  float lo = first ? v.x : INFINITY, hi = first ? v.x : -INFINITY;
+  const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (k == 0 && first) continue;
+    lo = (e[k] < lo) ? e[k] : lo;
+    hi = (hi < e[k]) ? e[k] : hi;
+  }
+  for (int off = 1; off < lpg; off <<= 1) {
+    const float plo = __shfl_xor_sync(0xffffffffu, lo, off);
+    const float phi = __shfl_xor_sync(0xffffffffu, hi, off);
+    const bool earlier = (li & off) == 0;
+    const float alo = earlier ? lo : plo, blo = earlier ? plo : lo;
+    const float ahi = earlier ? hi : phi, bhi = earlier ? phi : hi;
+    lo = (blo < alo) ? blo : alo;
+    hi = (ahi < bhi) ? bhi : ahi;
+  }
+  const int levels = FMT == KVF_FMT_INT8 ? 255 : 15;
+  const __half zero_h = __float2half_rn(lo);
+  float scale = __fdiv_rn(__fsub_rn(hi, lo), (float)levels);
+  if (scale <= 0.f) scale = 1.f;
+  const __half scale_h = __float2half_rn(scale);
+  const float zero = __half2float(zero_h);
+  const float sc = __half2float(scale_h);
+  if (!valid) return;
+  const int gpr = D / group;
+  if (first) meta[r * gpr + li / lpg] = (uint32_t)h_bits(scale_h) | ((uint32_t)h_bits(zero_h) << 16);
+  uint32_t c[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) c[k] = (uint32_t)code(e[k], zero, sc, levels);
+  if (FMT == KVF_FMT_INT8) {
+    reinterpret_cast<uint32_t *>(data + r * D)[li] = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+  } else {
+    reinterpret_cast<uint16_t *>(data + r * (D / 2))[li] = (uint16_t)(c[0] | (c[1] << 4) | (c[2] << 8) | (c[3] << 12));
+  }
+}
+
 __global__ void to_f16(const float *__restrict__ x, long long count, __half *__restrict__ out) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < count) out[i] = __float2half_rn(x[i]);
@@ -91,6 +151,26 @@ extern "C" cudaError_t kvf_b200_quantize(int fmt, int d, int group, const float 
   }
   if (group <= 0 || d % group || !meta) return cudaErrorInvalidValue;
   if ((fmt == KVF_FMT_INT4 && (group & 1))) return cudaErrorInvalidValue;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(data) & (fmt == KVF_FMT_INT8 ? 3u : 1u)) == 0;
+  if (group >= 4 && (group & (group - 1)) == 0 && aligned) {
+    // One warp per row (D = 128) or two (D = 64), 8 warps per block.
+    const long long warps = (rows * d / 4 + 31) / 32;
+    const unsigned blocks = (unsigned)((warps + 7) / 8);
+    if (fmt == KVF_FMT_INT8 && d == 128)
+      kvfb::quantize_rows<KVF_FMT_INT8, 128><<<blocks, 256, 0, stream>>>(x, rows, group, data,
+                                                                        reinterpret_cast<uint32_t *>(meta));
+    else if (fmt == KVF_FMT_INT8)
+      kvfb::quantize_rows<KVF_FMT_INT8, 64><<<blocks, 256, 0, stream>>>(x, rows, group, data,
+                                                                       reinterpret_cast<uint32_t *>(meta));
+    else if (d == 128)
+      kvfb::quantize_rows<KVF_FMT_INT4, 128><<<blocks, 256, 0, stream>>>(x, rows, group, data,
+                                                                        reinterpret_cast<uint32_t *>(meta));
+    else
+      kvfb::quantize_rows<KVF_FMT_INT4, 64><<<blocks, 256, 0, stream>>>(x, rows, group, data,
+                                                                       reinterpret_cast<uint32_t *>(meta));
+    return cudaGetLastError();
+  }
   const long long threads = rows * (d / group);
   const unsigned blocks = (unsigned)((threads + 127) / 128);
   if (fmt == KVF_FMT_INT8)
