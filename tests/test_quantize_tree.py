@@ -1,12 +1,12 @@
 """The device quantizer combines a group's min and max across lanes
-(quantize.cu, quantize_rows); the host quantizer folds them in one loop
-(runtime/kvf_host.h:91-95: std::min / std::max, i.e. lo = v < lo ? v : lo and
-hi = hi < v ? v : hi, from
-the first element). This restates the lane scheme in numpy float32 (4
-channels per lane, +inf/-inf start on lanes without the first element, an
-xor tree that combines the earlier range first) and checks that it gives the
-loop's bits for groups of 4..128 channels with NaN, +-inf and +-0 mixed in.
-The GPU tests check the kernel's bytes against the reference quantizer."""
+(quantize.cu, quantize_rows); the host quantizer folds them in one loop from
+the first element (runtime/kvf_host.h:91-95: std::min / std::max, i.e.
+lo = v < lo ? v : lo and hi = hi < v ? v : hi). This restates the lane
+scheme in numpy float32 (4 channels per lane, +inf/-inf start on lanes
+without the first element, an xor tree that combines the earlier range
+first) and checks that it gives the loop's bits for groups of 4..128
+channels with NaN, +-inf and +-0 mixed in. The GPU tests check the kernel's
+bytes against the reference quantizer."""
 from __future__ import annotations
 
 import numpy as np
