@@ -1,22 +1,26 @@
 """Decode-attention benchmark: us per decode step and effective KV TB/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+    python bench.py --op quantize [--workload NAME]     # the device KV quantizer, one GPU
 
 One JSON line on rank 0. A "step" is one decode step of one layer over the
 workload's KV cache (the kernel plus the split merge), with L2 flushed before
 every step: a write of 3 x L2, as the reference times it
 (runtime/kvf_host.h:302-330), then a read of 3 x L2 from a second buffer, so
 that the step does not also write the flush's dirty lines back to HBM (the
-line's "write_flush" gives the step after the write alone). The payload is 2 * rows * (row bytes + 4 * groups)
-(runtime/kvf_driver.cu:51) over the stored tokens; value = payload of all
-ranks / max-over-ranks step time, in TB/s.
+line's "write_flush" gives the step after the write alone). The payload is
+2 * rows * (row bytes + 4 * groups) (runtime/kvf_driver.cu:51) over the
+stored tokens; value = payload of all ranks / max-over-ranks step time, in
+TB/s.
 
   value   device time of the step, inputs resident in HBM, CUDA events on the
           launching stream
-  e2e     the same step through the public API (kvf_b200_decode) with the query
-          copied in from pinned host memory and the output copied back, inside
-          the timed region; the KV cache itself stays resident, as a decode cache
-          does
+  e2e     the same step through the public API with host buffers, inside the
+          timed region: api.Decoder replays the step as a CUDA graph whose
+          first kernel reads the queries from pinned host memory and whose
+          last writes the output into pinned host memory (sharded workloads:
+          copies of the queries in and the output out around the step); the
+          KV cache itself stays resident, as a decode cache does
   --impl reference
           the reference's own CPU implementation of the path,
           kvf::reference_attention (runtime/kvf_host.h:202-234, compiled
@@ -28,8 +32,10 @@ workloads the reference does not shard, the headline among them, run as N
 independent replicas (weak scaling, no collective). The two sharded
 workloads split one problem over the N GPUs (strong scaling):
   long_gqa_b1_n65536_int4g32_hm         split-KV: each GPU decodes its token
-                                        range, one NCCL all-gather of the
-                                        (output, lse) states, merge_states kernel
+                                        range; the (output, lse) states cross
+                                        NVLink inside the split-merge kernel
+                                        (--exchange fused; or separate NVLink
+                                        kernels, or an NCCL all-gather)
   llama3_70b_b64_n16384_int8g64_tm_p16  KV heads: each GPU owns Hkv/N KV heads of
                                         every sequence; no exchange (the
                                         all-gather of the outputs is timed
