@@ -36,13 +36,15 @@ enum { KVFO_HEAD = 0, KVFO_TOKEN = 1 };
 static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 
-/* IEEE binary32 -> binary16, round to nearest, ties to even. */
+/* IEEE binary32 -> binary16, round to nearest, ties to even. Every NaN
+ * becomes 0x7fff whatever its sign and payload, as the reference's host
+ * conversion gives (checked against oracle/_ref in tests/test_oracle.py). */
 uint16_t kvfo_f2h(float f) {
   const uint32_t x = f2u(f);
   const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
   const uint32_t ax = x & 0x7fffffffu;
-  if (ax >= 0x7f800000u) /* inf, nan */
-    return (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u));
+  if (ax > 0x7f800000u) return 0x7fffu; /* nan */
+  if (ax == 0x7f800000u) return (uint16_t)(sign | 0x7c00u); /* inf */
   const int e = (int)(ax >> 23);
   if (e >= 143) return (uint16_t)(sign | 0x7c00u); /* >= 2^16: overflow */
   if (e >= 113) { /* normal half: biased half exponent e - 112 in [1, 30] */
@@ -65,11 +67,13 @@ uint16_t kvfo_f2h(float f) {
   }
 }
 
+/* binary16 -> binary32, exact; a NaN becomes 0x7fffffff, as the reference's
+ * host conversion gives. */
 float kvfo_h2f(uint16_t h) {
   const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
   const uint32_t e = (h >> 10) & 0x1fu;
   uint32_t m = h & 0x3ffu;
-  if (e == 0x1f) return u2f(sign | 0x7f800000u | (m << 13));
+  if (e == 0x1f) return m ? u2f(0x7fffffffu) : u2f(sign | 0x7f800000u);
   if (e == 0) {
     if (m == 0) return u2f(sign);
     /* subnormal: normalise */

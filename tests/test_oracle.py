@@ -51,6 +51,35 @@ def test_f16_bits_match_reference():
     assert np.array_equal(O.h2f(bits).view(np.uint32), f["deq"].view(np.uint32))
 
 
+@pytest.mark.parametrize("name", list(FORMATS))
+def test_quantize_matches_reference_on_special_values(name):
+    """NaN (any sign and payload, first in a group and inside one), +-inf,
+    +-0 and values beyond the fp16 range, against the reference's own
+    kvf::quantize built from its sources (oracle/_ref): codes, metadata words
+    and dequantised values bit for bit."""
+    if not O.Ref.available():
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    fmt, group = FORMATS[name]
+    rs = np.random.RandomState(7)
+    specials = np.array([0x7fc00000, 0xffc00000, 0x7f800001, 0xff800001, 0x7fffffff, 0x7f800000, 0xff800000,
+                         0x00000000, 0x80000000, 0x49742400, 0xc9742400, 0x477fe000, 0x477ff000],
+                        dtype=np.uint32).view(np.float32)
+    for d in (64, 128):
+        if group > d:
+            continue
+        X = rs.standard_normal((256, d)).astype(np.float32)
+        m = rs.rand(*X.shape) < 0.05
+        X[m] = rs.choice(specials, int(m.sum()))
+        X[::7, 0] = np.nan
+        X[::5, d // 2 + 1] = -np.nan
+        got = O.quantize(fmt, d, group, X)
+        want = O.Ref.quantize(fmt, d, group, X)
+        for g_, w_ in zip(got, want):
+            if g_ is None:
+                continue
+            assert np.array_equal(np.asarray(g_).view(np.uint8), np.asarray(w_).view(np.uint8)), (name, d)
+
+
 @pytest.mark.parametrize("key", [f"{n}_d{d}" for n in FORMATS if n != "f16" for d in (64, 128)
                                  if FORMATS[n][1] <= d])
 def test_quantize_matches_reference(qfix, key):
