@@ -114,6 +114,32 @@ def test_quantize_bit_exact(cuda, fmt, group, d):
     assert np.array_equal(data.cpu().numpy()[:n0], qfix[f"{name}:{group}_d{d}/data"])
 
 
+@pytest.mark.parametrize("fmt,group", [(FMT_F16, 0), (FMT_INT8, 64), (FMT_INT8, 128), (FMT_INT4, 32),
+                                       (FMT_INT4, 128)])
+@pytest.mark.parametrize("d", [64, 128])
+def test_quantize_special_values_bit_exact(cuda, fmt, group, d):
+    """Rows with NaN (any sign and payload, first in a group and inside one),
+    +-inf, +-0 and values beyond the fp16 range: the device bytes and
+    metadata equal the oracle's, which the CPU tests pin to the reference's
+    own quantizer on the same kind of rows."""
+    if group > d:
+        pytest.skip("group larger than the row")
+    rs = np.random.RandomState(d + group + 5)
+    specials = np.array([0x7fc00000, 0xffc00000, 0x7f800001, 0xff800001, 0x7fffffff, 0x7f800000, 0xff800000,
+                         0x00000000, 0x80000000, 0x49742400, 0xc9742400, 0x477fe000, 0x477ff000],
+                        dtype=np.uint32).view(np.float32)
+    X = rs.standard_normal((512, d)).astype(np.float32)
+    m = rs.rand(*X.shape) < 0.05
+    X[m] = rs.choice(specials, int(m.sum()))
+    X[::7, 0] = np.nan
+    X[::5, d // 2 + 1] = -np.nan
+    data, meta = api.quantize(torch.as_tensor(X, device=cuda), fmt, group)
+    rd, rm, _ = O.quantize(fmt, d, group, X)
+    assert np.array_equal(data.cpu().numpy().view(np.uint8), np.asarray(rd).view(np.uint8).reshape(data.shape))
+    if meta is not None:
+        assert np.array_equal(meta.cpu().numpy().view(np.uint32), rm)
+
+
 def test_quantize_f16_bits(cuda):
     f = np.load(GOLDEN / "f16.npz")
     data, meta = api.quantize(torch.as_tensor(f["x"].reshape(-1, 64), device=cuda), FMT_F16)
