@@ -181,7 +181,7 @@ typedef struct kvf_exchange {
 
 /* kvf_b200_decode over this rank's tokens with the cross-GPU combination
  * fused into the split merge (a->splits must be > 1; split_sem is ignored).
- * A wait that runs out of time zeroes its slice and sets bit 2 of
+ * A wait that runs out of time zeroes its slice and sets bit 1 (value 2) of
  * kvf_b200_device_errors(). */
 cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
                                      const kvf_exchange *x, cudaStream_t stream);

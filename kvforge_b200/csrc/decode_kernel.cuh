@@ -304,6 +304,17 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
+// warp_wait for one thread (an MMA issuer): mbarrier.try_wait sleeps in
+// hardware between checks, so the waiting thread takes few issue slots.
+__device__ __forceinline__ bool thread_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0 && (*abort_flag || ptx::globaltimer_ns() - t0 > 2000000000ull)) return false;
+  }
+}
+
 // 2^e as a float, for e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 

@@ -6,24 +6,56 @@
   oracle/_ref/libkvf_ref.so       the reference's own host functions
                                   (runtime/kvf_host.h, via oracle/ref_shim.cu),
                                   built only where the reference tree exists
+  oracle/_ref/harness/            the reference's own harnesses built against
+                                  this library's drop-in headers (include/):
+                                  kvf_driver_<plan> (runtime/kvf_driver.cu with
+                                  each plan the reference's compiler emitted
+                                  under results/plans/, and one plan emitted by
+                                  kvforge_b200.codegen), kvf_sweep
+                                  (bench/sweep.cu over the dispatch tables
+                                  kvforge_b200.codegen emits) and the plans
+                                  file the sweep test times
 
-Neither output is committed (.gitignore); both travel with the working tree
-to the GPU box, where the reference tree itself is absent. The reference's
-own build system (CMake, PowerShell) is not used: the one header needed is
-compiled directly, unmodified, from where it lies.
+None of the outputs is committed (.gitignore); all travel with the working
+tree to the GPU box, where the reference tree itself is absent. The
+reference's own build system (CMake, PowerShell) is not used: the few files
+needed are compiled directly, unmodified, from where they lie.
+
+The reference tree is found through the KVF_REFERENCE environment variable,
+else BASELINE.json's "reference_path"; without either, only the restatement
+is built.
 """
 from __future__ import annotations
 
+import csv
+import json
 import os
 import shutil
 import subprocess
 import sys
+import tempfile
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("KVF_REFERENCE", "/root/reference"))
+REPO = HERE.parent
 ORACLE_SO = HERE / "_build" / "libkvf_oracle.so"
 REF_SO = HERE / "_ref" / "libkvf_ref.so"
+HARNESS = HERE / "_ref" / "harness"
+
+
+def reference_root() -> Path | None:
+    env = os.environ.get("KVF_REFERENCE")
+    if env:
+        return Path(env)
+    baseline = REPO / "BASELINE.json"
+    if baseline.exists():
+        p = json.loads(baseline.read_text()).get("reference_path")
+        if p:
+            return Path(p)
+    return None
+
+
+REFERENCE = reference_root()
 
 
 def _stale(out: Path, deps) -> bool:
@@ -47,7 +79,7 @@ def build_oracle(force: bool = False) -> Path:
 
 
 def reference_available() -> bool:
-    return (REFERENCE / "runtime" / "kvf_host.h").exists()
+    return REFERENCE is not None and (REFERENCE / "runtime" / "kvf_host.h").exists()
 
 
 def build_reference(force: bool = False) -> Path | None:
@@ -67,9 +99,126 @@ def build_reference(force: bool = False) -> Path | None:
     return REF_SO
 
 
+# The sweep test times a few plans of this reference shape for every kind of
+# variant id (format x order x residency), taken from the reference's own
+# candidate list.
+SWEEP_SHAPE = "gqa4_8k"
+SWEEP_PER_KIND = 2
+# A plan kvforge_b200.codegen emits (cost-model choice of splits and kernel
+# path) for the reference driver: the Llama-3-70B-shape batch cut to 4
+# sequences of 4096 tokens, int8 groups of 64, token-major pages of 16.
+CODEGEN_PLAN = dict(name="llama3_70b_b4_n4096", B=4, H=64, Hkv=8, d=128, n=4096, fmt=1, group=64, order=1,
+                    paged=True, block_tokens=16)
+
+
+def _overlay(links: dict) -> Path:
+    """A temporary directory of symbolic links, so that a reference source
+    that includes "kvf_kernels.cuh" next to itself finds this library's
+    drop-in header instead of the reference's kernels."""
+    d = Path(tempfile.mkdtemp(prefix="kvf_harness_"))
+    for name, target in links.items():
+        (d / name).symlink_to(Path(target).resolve())
+    return d
+
+
+def build_harnesses(force: bool = False) -> list:
+    """Compile the reference's driver and sweep harnesses, unmodified, against
+    include/ and libkvforge_b200.so. Returns the binaries built (or found)."""
+    if not reference_available():
+        return sorted(HARNESS.glob("kvf_*")) if HARNESS.exists() else []
+    lib = REPO / "kvforge_b200" / "_lib" / "libkvforge_b200.so"
+    if not lib.exists():
+        return []
+    HARNESS.mkdir(parents=True, exist_ok=True)
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    inc = REPO / "include"
+    common = {
+        "kvf_kernels.cuh": inc / "kvf_kernels.cuh",
+        "kvforge_b200.h": inc / "kvforge_b200.h",
+        "kvf_host.h": REFERENCE / "runtime" / "kvf_host.h",
+        "kvf_registry.h": REFERENCE / "runtime" / "kvf_registry.h",
+    }
+    cflags = [nvcc, "-std=c++17", "-O2", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler",
+              "-ffp-contract=off"]
+    lflags = ["-L", str(lib.parent), "-lkvforge_b200", "-Xlinker", "-rpath,$ORIGIN/../../../kvforge_b200/_lib"]
+    deps_common = [lib, *common.values()]
+    built = []
+
+    # Drivers: runtime/kvf_driver.cu with one emitted plan each.
+    plans = []
+    for info in sorted((REFERENCE / "results" / "plans").glob("*/plan_info.h")):
+        name = info.parent.name
+        src = info.parent / f"decode_{name}.cu"
+        if src.exists():
+            plans.append((name, info, src))
+    # Emitted sources are kept (written only when their text changes), so an
+    # unchanged emission does not trigger a rebuild.
+    gen_dir = HARNESS / "gen"
+    gen_dir.mkdir(exist_ok=True)
+
+    def emit(fname: str, text: str) -> Path:
+        path = gen_dir / fname
+        if not path.exists() or path.read_text() != text:
+            path.write_text(text)
+        return path
+
+    sys.path.insert(0, str(REPO))
+    from kvforge_b200 import codegen
+
+    p = codegen.plan(**CODEGEN_PLAN)
+    src = emit(f"decode_{p.name}.cu", codegen.emit_kernel_source(p))
+    info = emit(f"plan_info_{p.name}.h", codegen.emit_plan_header(p))
+    plans.append((f"codegen_{p.name}", info, src))
+    for name, info, src in plans:
+        out = HARNESS / f"kvf_driver_{name}"
+        deps = deps_common + [REFERENCE / "runtime" / "kvf_driver.cu", info, src]
+        if force or _stale(out, deps):
+            ov = _overlay({**common, "kvf_driver.cu": REFERENCE / "runtime" / "kvf_driver.cu",
+                           "plan_info.h": info, src.name: src})
+            try:
+                _run(cflags + [f"-I{ov}", f"-I{inc}", str(ov / "kvf_driver.cu"), str(ov / src.name), "-o",
+                               str(out)] + lflags)
+            finally:
+                shutil.rmtree(ov, ignore_errors=True)
+        built.append(out)
+
+    # Sweep: bench/sweep.cu over the emitted sm_100a dispatch tables.
+    tables = [emit(fname, text) for fname, text in codegen.emit_dispatch_sources()]
+    out = HARNESS / "kvf_sweep"
+    if force or _stale(out, deps_common + [REFERENCE / "bench" / "sweep.cu", *tables]):
+        ov = _overlay({**common, "sweep.cu": REFERENCE / "bench" / "sweep.cu", **{t.name: t for t in tables}})
+        try:
+            _run(cflags + [f"-I{ov}", f"-I{inc}", str(ov / "sweep.cu"), *[str(ov / t.name) for t in tables],
+                           "-o", str(out)] + lflags)
+        finally:
+            shutil.rmtree(ov, ignore_errors=True)
+    built.append(out)
+
+    # The plans the sweep test times.
+    src_csv = REFERENCE / "results" / "plans" / SWEEP_SHAPE / "plans.csv"
+    sel = HARNESS / f"plans_{SWEEP_SHAPE}.csv"
+    if src_csv.exists() and (force or _stale(sel, [src_csv])):
+        with open(src_csv, newline="") as f:
+            rows = list(csv.reader(f))
+        head, body = rows[0], rows[1:]
+        col = {h: i for i, h in enumerate(head)}
+        picked = {}  # kind -> [(split/pack/page configuration, row)], distinct configurations
+        for r in body:
+            kind = (r[col["fmt"]], r[col["order"]], r[col["residency"]])
+            cfg = (r[col["splits"]], r[col["gqa_pack"]], r[col["block_tokens"]])
+            lst = picked.setdefault(kind, [])
+            if len(lst) < SWEEP_PER_KIND and all(cfg != c for c, _ in lst):
+                lst.append((cfg, r))
+        keep = [r for lst in picked.values() for _, r in lst]
+        with open(sel, "w", newline="") as f:
+            csv.writer(f, lineterminator="\n").writerows([head] + keep)
+    return built
+
+
 def build(force: bool = False) -> None:
     build_oracle(force)
     build_reference(force)
+    build_harnesses(force)
 
 
 if __name__ == "__main__":
