@@ -13,7 +13,10 @@
  * Error behaviour follows the reference launcher (runtime/kvf_kernels.cuh:309-320):
  * every entry point returns a cudaError_t, never throws, never synchronises
  * and never exits. Launches are stream-ordered; the library holds no state
- * between calls apart from cached driver entry points.
+ * between calls apart from caches of driver facts: driver entry points, SM
+ * counts, and per CUDA context each kernel's shared-memory attribute and
+ * occupancy (a context that replaces another, after cudaDeviceReset, starts
+ * with empty caches).
  */
 #ifndef KVFORGE_B200_H
 #define KVFORGE_B200_H
@@ -115,22 +118,39 @@ cudaError_t kvf_b200_decode(const kvf_args *a, int fmt, int d, int g, int ord, i
  * "mma on/off" choice):
  *   KVF_PATH_AUTO  by shape: the tcgen05 kernel for int8 rows of 128
  *                  dimensions with one or two quantization groups once there
- *                  are >= 32 (sequence, KV head) units, else mma.sync; the
- *                  environment variable KVF_B200_TC=1/0 forces one of them;
+ *                  are >= 32 (sequence, KV head) units, else mma.sync;
  *   KVF_PATH_MMA   always the mma.sync kernel (every format);
  *   KVF_PATH_TC    always the tcgen05 kernel; shapes it does not cover return
  *                  cudaErrorNotSupported without launching. */
 enum { KVF_PATH_AUTO = 0, KVF_PATH_MMA = 1, KVF_PATH_TC = 2 };
 
-/* kvf_b200_decode on an explicit kernel path (KVF_PATH_*); any other path
- * value returns cudaErrorInvalidValue. kvf_b200_decode is path AUTO. */
+/* Scheduling flags, OR'ed into a path value. They choose how the mma.sync
+ * launch is organised, not what it computes: every combination gives the
+ * same output (the two merge schemes bit for bit).
+ *   KVF_FLAG_MERGE_KERNEL  the split merge runs as its own kernel, even where
+ *                          the launch would merge after a grid barrier;
+ *   KVF_FLAG_GRID_MERGE    the grid-barrier merge wherever it is possible
+ *                          (split_sem given, at least two (sequence, KV head)
+ *                          units, every block resident), not only where it
+ *                          measured faster (two or more merge slices per
+ *                          decode block);
+ *   KVF_FLAG_NO_BALANCE    one split count for every sequence even when
+ *                          seq_lens is given (the reference's schedule).
+ * MERGE_KERNEL and GRID_MERGE together, or any other bit, is
+ * cudaErrorInvalidValue. */
+enum { KVF_FLAG_MERGE_KERNEL = 0x100, KVF_FLAG_GRID_MERGE = 0x200, KVF_FLAG_NO_BALANCE = 0x400 };
+
+/* kvf_b200_decode on an explicit kernel path: path is KVF_PATH_*, optionally
+ * OR'ed with KVF_FLAG_* bits; any other value returns cudaErrorInvalidValue.
+ * kvf_b200_decode is path AUTO with no flags. */
 cudaError_t kvf_b200_decode_path(const kvf_args *a, int fmt, int d, int g, int ord, int paged, int path,
                                  cudaStream_t stream);
 
 /* One decode step whose queries come from host memory, with no copy-engine
  * transfer: a small kernel reads q_host (B*H*d floats, 16-byte aligned, in
  * pinned host memory the device addresses at the same pointer, e.g. from
- * cudaHostAlloc) into a->q, and the decode (on `path`, KVF_PATH_*) is launched
+ * cudaHostAlloc) into a->q, and the decode (on `path`, as kvf_b200_decode_path
+ * takes it) is launched
  * as its programmatic dependent, so the K/V stream starts while the queries
  * are still in flight; the decode reads them only once the copy kernel has
  * completed. a->out (and a->lse) may likewise point at such host memory: the
@@ -245,7 +265,7 @@ int kvf_b200_suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int gr
  * sequence can use under balanced splits, within 64 MiB of partials; the
  * same as kvf_b200_suggest_splits where the launch does not balance
  * (tensor-core path, or more (sequence, head group) units than one wave of
- * blocks). Environment: KVF_B200_BALANCE=0 turns balancing off. */
+ * blocks). */
 int kvf_b200_suggest_splits_ragged(int B, int H, int Hkv, int n, int fmt, int d, int group, int paged,
                                    int block_tokens);
 /* The chunk (tokens per split) a balanced launch uses, computed on the host
@@ -263,7 +283,8 @@ int kvf_b200_balanced_chunk(const int *seq_lens, int B, int n, int splits, int u
  * launching anything. */
 cudaError_t kvf_b200_describe(const kvf_args *a, int fmt, int d, int ord, int paged, char *buf,
                               int buf_len);
-/* kvf_b200_describe for an explicit kernel path (KVF_PATH_*). */
+/* kvf_b200_describe for an explicit kernel path (KVF_PATH_* with optional
+ * KVF_FLAG_* bits, as kvf_b200_decode_path takes it). */
 cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d, int ord, int paged, int path, char *buf,
                                    int buf_len);
 
@@ -305,8 +326,9 @@ cudaError_t kvf_b200_quantize(int fmt, int d, int group, const float *x, long lo
  *     Nothing needs clearing between calls: every call writes each partial
  *     it later reads;
  *   - the first call on each device looks up the array's device address
- *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
+ *     (cudaGetSymbolAddress, with that device current), and looks it up
+ *     again if the device's context was replaced (cudaDeviceReset); make
+ *     that first call before any stream capture.
  * splits <= 1 needs no scratch and behaves exactly like kvf_b200_decode. */
 cudaError_t kvf_b200_decode_noalloc(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
                                     cudaStream_t stream);

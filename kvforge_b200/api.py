@@ -193,24 +193,29 @@ def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace)
 
 
 PATHS = {"auto": 0, "mma": 1, "tc": 2}  # KVF_PATH_AUTO / KVF_PATH_MMA / KVF_PATH_TC
+# Scheduling flags (KVF_FLAG_*), OR'ed into the path value: how the mma.sync
+# launch merges its splits and whether it balances ragged batches; the output
+# is the same whichever are set.
+FLAG_MERGE_KERNEL, FLAG_GRID_MERGE, FLAG_NO_BALANCE = 0x100, 0x200, 0x400
 
 
-def _path(path: str) -> int:
+def _path(path: str, flags: int = 0) -> int:
     if path not in PATHS:
         raise ValueError(f"path must be one of {sorted(PATHS)}")
-    return PATHS[path]
+    return PATHS[path] | int(flags)
 
 
 def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = None,
            splits: Optional[int] = None, workspace: Optional[Workspace] = None, stream=None,
-           g: int = 1, lse: Optional[torch.Tensor] = None, path: str = "auto") -> torch.Tensor:
+           g: int = 1, lse: Optional[torch.Tensor] = None, path: str = "auto", flags: int = 0) -> torch.Tensor:
     """One decode step: out[b][h] = softmax(q k^T * scale) v over the cache.
 
     q: float32 [B][H][D] on the cache's device. Returns out (float32 [B][H][D]).
     lse (optional float32 [B][H]) receives log2 of each head's softmax
     denominator, for combining outputs over disjoint token ranges with
     merge_states. path: "auto" (the launcher chooses), "mma" (mma.sync
-    kernel) or "tc" (tcgen05 kernel; int8 rows of 128 only)."""
+    kernel) or "tc" (tcgen05 kernel; int8 rows of 128 only); flags: FLAG_*
+    scheduling bits."""
     if q.dtype != torch.float32 or not q.is_contiguous():
         raise ValueError("q must be a contiguous float32 tensor [B][H][D]")
     B, H, d = q.shape
@@ -227,7 +232,7 @@ def decode(q: torch.Tensor, cache: KVCache, *, out: Optional[torch.Tensor] = Non
     check(
         "kvf_b200_decode_path",
         lib().kvf_b200_decode_path(ctypes.byref(a), cache.fmt, d, g, cache.place.order,
-                                   int(cache.place.paged), _path(path), _stream(stream)),
+                                   int(cache.place.paged), _path(path, flags), _stream(stream)),
     )
     return out
 
@@ -254,7 +259,7 @@ class Decoder:
     """
 
     def __init__(self, cache: KVCache, H: int, *, splits: Optional[int] = None, path: str = "auto",
-                 g: int = 1, graph: bool = True, zero_copy: bool = True):
+                 g: int = 1, graph: bool = True, zero_copy: bool = True, flags: int = 0):
         dev = cache.k.device
         B, d = cache.B, cache.d
         self.cache = cache
@@ -268,7 +273,7 @@ class Decoder:
         self._args = make_args(self.q, cache, self.out, self.workspace)
         if zero_copy:
             self._args.out = self.out_host.data_ptr()
-        self._code = (cache.fmt, d, g, cache.place.order, int(cache.place.paged), _path(path))
+        self._code = (cache.fmt, d, g, cache.place.order, int(cache.place.paged), _path(path, flags))
         self.graph = None
         if graph:
             # Warm up outside the capture (first launches set kernel attributes).
@@ -331,7 +336,7 @@ def merge_states(outs: torch.Tensor, lses: torch.Tensor, out: Optional[torch.Ten
     return out
 
 
-def describe(q: torch.Tensor, cache: KVCache, workspace: Workspace, path: str = "auto") -> str:
+def describe(q: torch.Tensor, cache: KVCache, workspace: Workspace, path: str = "auto", flags: int = 0) -> str:
     """One line describing the launch decode() would make (kernel, grid,
     stages, shared memory, splits), without launching."""
     B, H, d = q.shape
@@ -339,7 +344,7 @@ def describe(q: torch.Tensor, cache: KVCache, workspace: Workspace, path: str = 
     buf = ctypes.create_string_buffer(512)
     check("kvf_b200_describe_path",
           lib().kvf_b200_describe_path(ctypes.byref(a), cache.fmt, d, cache.place.order,
-                                       int(cache.place.paged), _path(path), buf, 512))
+                                       int(cache.place.paged), _path(path, flags), buf, 512))
     return buf.value.decode()
 
 
@@ -347,5 +352,6 @@ def device_errors() -> int:
     return int(lib().kvf_b200_device_errors())
 
 
-__all__ = ["KVCache", "Workspace", "Decoder", "decode", "PATHS", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
+__all__ = ["KVCache", "Workspace", "Decoder", "decode", "PATHS", "FLAG_MERGE_KERNEL", "FLAG_GRID_MERGE",
+           "FLAG_NO_BALANCE", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
            "device_errors", "row_bytes", "groups_per_row", "scale_log2", "FMT_F16", "FMT_INT8", "FMT_INT4"]

@@ -414,13 +414,6 @@ void *tc_kernel_for(int gpr, int nh) {
   return nullptr;
 }
 
-// KVF_B200_TC=0 in the environment selects the mma.sync kernels for every
-// format (for A/B measurements); the default uses tcgen05 where it applies.
-bool tc_enabled() {
-  const char *e = std::getenv("KVF_B200_TC");
-  return !(e && e[0] == '0');
-}
-
 uint32_t tc_misc_bytes(int gpr, int nh) {
   size_t n = 0;
   if (gpr == 1) n = nh == 4 ? sizeof(TcMisc<1, 4>) : sizeof(TcMisc<1, 8>);
@@ -432,23 +425,25 @@ uint32_t tc_misc_bytes(int gpr, int nh) {
 // enough (sequence, KV head) units to fill the GPU without many splits. The
 // B200 sweep (machines/b200-sxm.sweep.csv) puts the crossover between 8 units
 // (mma.sync 25.6 us vs 30.8 us) and 32 units (tcgen05 43.1 us vs 45.9 us).
-// KVF_B200_TC=1 forces it for every shape it supports, KVF_B200_TC=0 never.
+// KVF_PATH_TC forces it for every shape it supports, KVF_PATH_MMA never.
 constexpr int kTcMinUnits = 32;
 
 bool tc_supported(const Shape &sh) { return sh.fmt == 1 && sh.d == 128 && (sh.gpr == 1 || sh.gpr == 2); }
 
-bool tc_applies(const Shape &sh, int units) {
-  const char *e = std::getenv("KVF_B200_TC");
-  const bool forced = e && e[0] == '1';
-  if (!tc_enabled() || !tc_supported(sh)) return false;
-  return forced || units >= kTcMinUnits;
-}
+bool tc_applies(const Shape &sh, int units) { return tc_supported(sh) && units >= kTcMinUnits; }
+
+constexpr int kPathMask = 0xFF;
+constexpr int kFlagMask = KVF_FLAG_MERGE_KERNEL | KVF_FLAG_GRID_MERGE | KVF_FLAG_NO_BALANCE;
 
 // The kernel a launch on `path` runs: 1 = mma.sync, 2 = tcgen05; an error
-// status for a path value that does not exist or a tcgen05 request the shape
-// does not allow.
+// status for a path value that does not exist, contradictory or unknown
+// flags, or a tcgen05 request the shape does not allow.
 cudaError_t resolve_path(const Shape &sh, int units, int path, int &kernel) {
-  switch (path) {
+  const int flags = path & ~kPathMask;
+  if ((flags & ~kFlagMask) ||
+      ((flags & KVF_FLAG_MERGE_KERNEL) && (flags & KVF_FLAG_GRID_MERGE)))
+    return cudaErrorInvalidValue;
+  switch (path & kPathMask) {
   case KVF_PATH_AUTO:
     kernel = tc_applies(sh, units) ? 2 : 1;
     return cudaSuccess;
@@ -556,6 +551,107 @@ cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint
   return cudaLaunchKernelExC(&cfg, fn, params);
 }
 
+// Identifier of the current CUDA context (cuCtxGetId), 0 when there is none
+// yet or the driver cannot tell. Per-context caches key on it, so a context
+// that replaced another (after cudaDeviceReset) never sees stale entries.
+unsigned long long context_id() {
+  typedef CUresult (*GetCurrentFn)(CUcontext *);
+  typedef CUresult (*GetIdFn)(CUcontext, unsigned long long *);
+  static std::once_flag once;
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(p);
+    cudaGetLastError();
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Per-context facts about a kernel: the dynamic shared memory it may use
+// (cudaFuncSetAttribute is called only when a launch needs more than was set)
+// and its resident blocks per SM for one (threads, shared memory) pair, so a
+// decode step does not pay these driver queries on every call.
+struct KernelCtxEntry {
+  void *fn;
+  unsigned long long ctx;
+  uint32_t smem_set;
+  int occ_threads;
+  uint32_t occ_smem;
+  int occ_blocks;
+};
+std::mutex g_kctx_mu;
+KernelCtxEntry g_kctx[128];
+int g_kctx_n = 0;
+
+KernelCtxEntry *kctx_find(void *fn, unsigned long long ctx) {
+  for (int i = 0; i < g_kctx_n; ++i)
+    if (g_kctx[i].fn == fn && g_kctx[i].ctx == ctx) return &g_kctx[i];
+  return nullptr;
+}
+
+KernelCtxEntry *kctx_add(void *fn, unsigned long long ctx) {
+  if (ctx == 0) return nullptr;
+  if (KernelCtxEntry *e = kctx_find(fn, ctx)) return e;
+  if (g_kctx_n == 128) return nullptr;  // full: no caching, every call asks the driver
+  g_kctx[g_kctx_n] = KernelCtxEntry{fn, ctx, 0u, 0, 0u, 0};
+  return &g_kctx[g_kctx_n++];
+}
+
+// Lets `fn` use `smem` bytes of dynamic shared memory.
+cudaError_t ensure_smem(void *fn, uint32_t smem) {
+  std::lock_guard<std::mutex> lock(g_kctx_mu);
+  const unsigned long long ctx = context_id();
+  if (ctx) {
+    KernelCtxEntry *e = kctx_find(fn, ctx);
+    if (e && e->smem_set >= smem) return cudaSuccess;
+  }
+  const cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (r != cudaSuccess) return r;
+  if (KernelCtxEntry *e = kctx_add(fn, context_id())) e->smem_set = std::max(e->smem_set, smem);
+  return cudaSuccess;
+}
+
+// Whether every block of the launch can be resident at once (required by a
+// cooperative launch).
+bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
+  // The occupancy of a block with this much dynamic shared memory counts only
+  // once the kernel may use it (set here too, so describing agrees with launching).
+  if (ensure_smem(fn, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int per_sm = -1;
+  {
+    std::lock_guard<std::mutex> lock(g_kctx_mu);
+    const KernelCtxEntry *e = kctx_find(fn, context_id());
+    if (e && e->occ_threads == threads && e->occ_smem == smem) per_sm = e->occ_blocks;
+  }
+  if (per_sm < 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    std::lock_guard<std::mutex> lock(g_kctx_mu);
+    if (KernelCtxEntry *e = kctx_add(fn, context_id())) {
+      e->occ_threads = threads;
+      e->occ_smem = smem;
+      e->occ_blocks = per_sm;
+    }
+  }
+  return blocks <= per_sm * sm_count();
+}
+
 // Whether a decode launch should merge its splits itself (cooperative launch,
 // grid barrier): partials to merge, split counters with room for the barrier
 // words (two or more (sequence, KV head) units); behind a programmatic
@@ -566,31 +662,14 @@ cudaError_t launch_params(void *fn, int blocks, int threads, void **params, uint
 // columns) for 288 decode blocks step in 53.7 us instead of 57.2, while
 // single sequences with 128 slices for ~295 blocks lose 1.4-2.5 us (the
 // cooperative launch costs more than the merge kernel it replaces). So by
-// default it is used from two slices per decode block; KVF_B200_COOP=1
-// forces it where possible, =0 never uses it.
-bool coop_wanted(const kvf_args *a, int d, long long blocks) {
+// default it is used from two slices per decode block; KVF_FLAG_GRID_MERGE
+// asks for it wherever possible, KVF_FLAG_MERGE_KERNEL never.
+bool coop_wanted(const kvf_args *a, int d, long long blocks, int flags) {
   if (a->splits <= 1 || !a->split_sem || (long long)a->B * a->Hkv < 2) return false;
-  const char *e = std::getenv("KVF_B200_COOP");
-  if (e && e[0] == '0') return false;
-  if (e && e[0] == '1') return true;
+  if (flags & KVF_FLAG_MERGE_KERNEL) return false;
+  if (flags & KVF_FLAG_GRID_MERGE) return true;
   const long long slices = (long long)a->B * a->H * ((d + 31) / 32);
   return slices >= 2LL * blocks;
-}
-
-// Whether every block of the launch can be resident at once (required by a
-// cooperative launch).
-bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
-  int dev = 0, sms = 0, per_sm = 0;
-  // The occupancy of a block with this much dynamic shared memory counts only
-  // once the kernel may use it (set here too, so describing agrees with launching).
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return blocks <= per_sm * sms;
 }
 
 
@@ -605,19 +684,19 @@ bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
 // all, the long sequence had 36 of 296 blocks); 2k-8k tokens each, which
 // already streams at the batch's aggregate rate, 52.1 instead of 50.1. The
 // in-launch merge and the balanced splits need the general kernel;
-// contiguous caches without either run the lean one.
-cudaError_t plan_mma(const kvf_args *a, const Shape &sh, int d, const kvf_exchange *x, Launch &L, bool &want_coop) {
+// contiguous caches without either run the lean one. flags: KVF_FLAG_* bits.
+cudaError_t plan_mma(const kvf_args *a, const Shape &sh, int d, const kvf_exchange *x, int flags, Launch &L,
+                     bool &want_coop) {
   const int hh = heads_per_block(a->Hkv, sh.fmt, sh.d);
-  const char *env = std::getenv("KVF_B200_BALANCE");  // 0: one split count for all sequences
-  const bool bal_wanted = !x && a->seq_lens && a->splits > 1 && !(env && env[0] == '0');
-  want_coop = !x && coop_wanted(a, d, (long long)a->B * (a->Hkv / hh) * a->splits);
+  const bool bal_wanted = !x && a->seq_lens && a->splits > 1 && !(flags & KVF_FLAG_NO_BALANCE);
+  want_coop = !x && coop_wanted(a, d, (long long)a->B * (a->Hkv / hh) * a->splits, flags);
   cudaError_t e = plan_launch(a, sh, L, !sh.paged && !want_coop && !bal_wanted);
   if (e != cudaSuccess || !bal_wanted) return e;
   const long long slots = (long long)L.occupancy * sm_count();
   if ((long long)a->B * L.p.hg > slots) return cudaSuccess;
   L.p.bal_gran = (sh.paged && sh.bt > L.p.tb) ? sh.bt : L.p.tb;
   L.blocks = (int)std::min<long long>(slots, L.blocks);
-  want_coop = !x && coop_wanted(a, d, L.blocks);
+  want_coop = !x && coop_wanted(a, d, L.blocks, flags);
   return cudaSuccess;
 }
 
@@ -630,7 +709,7 @@ cudaError_t launch_tc(const kvf_args *a, const Shape &sh, cudaStream_t stream, c
   CUtensorMap tk, tv;
   e = encode_maps_box(a, sh, 128, 128, L.p.tbox, 1, tk, tv);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
+  e = ensure_smem(L.fn, L.p.smem_total);
   if (e != cudaSuccess) return e;
   const kvf_args args = *a;
   const TcPlan plan = L.p;
@@ -661,7 +740,7 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
   if (kernel == 2) return launch_tc(a, sh, stream, x, pdl);
   Launch L;
   bool want_coop = false;
-  e = plan_mma(a, sh, d, x, L, want_coop);
+  e = plan_mma(a, sh, d, x, path & ~kPathMask, L, want_coop);
   if (e != cudaSuccess) return e;
   CUtensorMap tk, tv, tkm, tvm;
   e = encode_maps(a, sh, L.p, tk, tv);
@@ -675,7 +754,7 @@ cudaError_t decode_impl(const kvf_args *a, int fmt, int d, int g, int ord, int p
     L.p.meta_ts = (uint32_t)(sh.gpr * 4);
     L.p.meta_hs = (uint32_t)(L.p.tb * sh.gpr * 4);
   }
-  e = cudaFuncSetAttribute(L.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.p.smem_total);
+  e = ensure_smem(L.fn, L.p.smem_total);
   if (e != cudaSuccess) return e;
   L.p.coop_merge = (want_coop && !L.p.final_out && coop_fits(L.fn, L.blocks, L.threads, L.p.smem_total)) ? 1 : 0;
   const kvf_args args = *a;
@@ -813,7 +892,7 @@ extern "C" cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d,
   }
   Launch L;
   bool want_coop = false;
-  e = plan_mma(a, sh, d, nullptr, L, want_coop);
+  e = plan_mma(a, sh, d, nullptr, path & ~kPathMask, L, want_coop);
   if (e != cudaSuccess) return e;
   if (buf && buf_len > 0) {
     const KernelInfo ki = info_for(L.fn);
@@ -910,8 +989,7 @@ int suggest_splits(int B, int H, int Hkv, int n, int fmt, int d, int group, int 
       best = s;
     }
   }
-  const char *env = std::getenv("KVF_B200_BALANCE");
-  if (ragged && !tc && units <= slots && best > 1 && !(env && env[0] == '0')) {
+  if (ragged && !tc && units <= slots && best > 1) {
     // Balanced launches (plan_mma) choose the chunk themselves; the split
     // count is the workspace's capacity per sequence. One sequence may use
     // up to slots / head-groups splits (when the others are short); the
@@ -985,12 +1063,15 @@ constexpr size_t kNoAllocScratchBytes = KVF_B200_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of the scratch array, looked up once per device with that
-// device current. In host code the array's name is only a host-side stand-in,
-// never a device address, so it is never passed to a kernel directly.
+// device current (and again if the device's context was replaced, e.g. after
+// cudaDeviceReset, which reloads the module). In host code the array's name is
+// only a host-side stand-in, never a device address, so it is never passed to
+// a kernel directly.
 void *noalloc_scratch_address(cudaError_t &err) {
   constexpr int kMaxDevices = 64;
   static std::mutex mu;
   static void *addr[kMaxDevices] = {};
+  static unsigned long long ctx_of[kMaxDevices] = {};
   int dev = 0;
   err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return nullptr;
@@ -999,11 +1080,12 @@ void *noalloc_scratch_address(cudaError_t &err) {
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  if (!addr[dev] || ctx_of[dev] != context_id()) {
     void *p = nullptr;
     err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (err != cudaSuccess) return nullptr;
     addr[dev] = p;
+    ctx_of[dev] = context_id();
   }
   err = cudaSuccess;
   return addr[dev];

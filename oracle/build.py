@@ -215,10 +215,77 @@ def build_harnesses(force: bool = False) -> list:
     return built
 
 
+# The reference's own decode kernels (its SIMT decode_partial + decode_merge,
+# runtime/kvf_kernels.cuh, compiled unmodified for sm_100a) in its driver, on
+# the five benchmark shapes, two split counts each: the CUDA-core baseline on
+# the same GPU. Config 3's ragged lengths become the uniform length with the
+# same total tokens (the reference has one n per batch); data is the
+# reference's own make_data (N(0,1)), as its driver generates it.
+REFGPU_PLANS = [
+    # name, B, H, Hkv, d, n, fmt, group, order, block_tokens, pack g, splits
+    ("cfg1_mha_b1_n4096_f16_hm", 1, 32, 32, 128, 4096, 0, 0, 0, 0, 1, (8, 16)),
+    ("cfg2_gqa_b1_n32768_int8g64_tm", 1, 32, 8, 128, 32768, 1, 64, 1, 0, 4, (64, 128)),
+    ("cfg3_gqa_b8_n5637_f16_tm_p16", 8, 32, 8, 128, 5637, 0, 0, 1, 16, 4, (8, 16)),
+    ("cfg4_gqa_b1_n65536_int4g32_hm", 1, 32, 8, 128, 65536, 2, 32, 0, 0, 4, (64, 128)),
+    ("cfg5_gqa_b64_n16384_int8g64_tm_p16", 64, 64, 8, 128, 16384, 1, 64, 1, 16, 8, (1, 2)),
+]
+
+
+def build_refgpu(force: bool = False) -> list:
+    """kvf_refgpu_<plan>_s<splits>: runtime/kvf_driver.cu with the reference's
+    own kvf_kernels.cuh (no file of this library involved), for sm_100a."""
+    if not reference_available():
+        return sorted(HARNESS.glob("kvf_refgpu_*")) if HARNESS.exists() else []
+    HARNESS.mkdir(parents=True, exist_ok=True)
+    gen_dir = HARNESS / "gen"
+    gen_dir.mkdir(exist_ok=True)
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    rt = REFERENCE / "runtime"
+    fmt_enum = {0: "kvf::FMT_F16", 1: "kvf::FMT_INT8", 2: "kvf::FMT_INT4"}
+    ord_enum = {0: "kvf::ORD_HEAD", 1: "kvf::ORD_TOKEN"}
+    built = []
+    for name, B, H, Hkv, d, n, fmt, group, order, bt, g, splits_list in REFGPU_PLANS:
+        for s in splits_list:
+            tag = f"{name}_s{s}"
+            src = f'''// Plan launcher in the form src/codegen.cpp:67-93 emits, for the reference's kernels.
+#include "kvf_kernels.cuh"
+extern "C" cudaError_t kvf_launch_{tag}(const kvf::Args *in, cudaStream_t st) {{
+  kvf::Args a = *in;
+  a.splits = {s};
+  a.warps = 4;
+  return kvf::launch<{fmt_enum[fmt]}, {d}, {g}, 2, {ord_enum[order]}, {"true" if bt else "false"}>(a, st);
+}}
+extern "C" const char *kvf_plan_{tag}() {{ return "{tag} (reference SIMT kernel)"; }}
+'''
+            hdr = (f"#pragma once\n#define KVF_LAUNCH kvf_launch_{tag}\n#define KVF_PLAN kvf_plan_{tag}\n"
+                   f"#define KVF_H {H}\n#define KVF_HKV {Hkv}\n#define KVF_D {d}\n#define KVF_N {n}\n"
+                   f"#define KVF_BATCH {B}\n#define KVF_FMT {fmt_enum[fmt]}\n#define KVF_GROUP {group}\n"
+                   f"#define KVF_ORDER {ord_enum[order]}\n#define KVF_PAGED {1 if bt else 0}\n"
+                   f"#define KVF_BLOCK {bt}\n#define KVF_SPLITS {s}\n#define KVF_WARPS 4\n#define KVF_PRED_US 0.0\n")
+            srcp, hdrp = gen_dir / f"refgpu_{tag}.cu", gen_dir / f"plan_info_refgpu_{tag}.h"
+            for path, text in ((srcp, src), (hdrp, hdr)):
+                if not path.exists() or path.read_text() != text:
+                    path.write_text(text)
+            out = HARNESS / f"kvf_refgpu_{tag}"
+            deps = [srcp, hdrp, rt / "kvf_driver.cu", rt / "kvf_host.h", rt / "kvf_kernels.cuh"]
+            if force or _stale(out, deps):
+                ov = _overlay({"kvf_kernels.cuh": rt / "kvf_kernels.cuh", "kvf_host.h": rt / "kvf_host.h",
+                               "kvf_driver.cu": rt / "kvf_driver.cu", "plan_info.h": hdrp, srcp.name: srcp})
+                try:
+                    _run([nvcc, "-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler",
+                          "-ffp-contract=off", f"-I{ov}", str(ov / "kvf_driver.cu"), str(ov / srcp.name), "-o",
+                          str(out)])
+                finally:
+                    shutil.rmtree(ov, ignore_errors=True)
+            built.append(out)
+    return built
+
+
 def build(force: bool = False) -> None:
     build_oracle(force)
     build_reference(force)
     build_harnesses(force)
+    build_refgpu(force)
 
 
 if __name__ == "__main__":

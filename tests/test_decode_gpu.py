@@ -25,7 +25,7 @@ torch = pytest.importorskip("torch")
 
 from kvforge_b200 import FMT_F16, FMT_INT4, FMT_INT8, ORD_HEAD, ORD_TOKEN  # noqa: E402
 from kvforge_b200 import api, workloads  # noqa: E402
-from kvforge_b200._native import check, lib  # noqa: E402
+from kvforge_b200._native import KvfError, check, lib  # noqa: E402
 from kvforge_b200.layout import Placement  # noqa: E402
 
 pytestmark = pytest.mark.gpu
@@ -48,7 +48,10 @@ def edge_inputs(shape, seed):
     return q, K, V
 
 
-def run(q, K, V, fmt, group, place, splits, seq_lens=None, variant=None, device="cuda:0", fused=True):
+def run(q, K, V, fmt, group, place, splits, seq_lens=None, variant=None, device="cuda:0", fused=True,
+        path="auto"):
+    """One decode through api.decode (variant None) or through the registry by
+    variant id; path "tc" / "mma" pins the kernel (the id gets its suffix)."""
     qd = torch.as_tensor(q, device=device)
     Kd = torch.as_tensor(K, device=device)
     Vd = torch.as_tensor(V, device=device)
@@ -56,11 +59,12 @@ def run(q, K, V, fmt, group, place, splits, seq_lens=None, variant=None, device=
     out = torch.full_like(qd, float("nan"))
     ws = api.Workspace.allocate(q.shape[0], q.shape[1], q.shape[2], splits, qd.device, fused=fused)
     if variant is None:
-        api.decode(qd, cache, out=out, workspace=ws)
+        api.decode(qd, cache, out=out, workspace=ws, path=path)
     else:
         a = api.make_args(qd, cache, out, ws)
+        vid = variant + {"auto": "", "tc": "_tc", "mma": "_mma"}[path]
         check("kvf_b200_launch_variant",
-              lib().kvf_b200_launch_variant(variant.encode(), ctypes.byref(a),
+              lib().kvf_b200_launch_variant(vid.encode(), ctypes.byref(a),
                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
     return out.cpu().numpy()
@@ -70,16 +74,19 @@ INT8_128 = {"f16": False, "int8": True, "int4": False}
 
 
 @pytest.fixture(params=["auto", "tcgen05", "mma.sync"])
-def kernel_path(request, monkeypatch):
-    """Runs a test on the default kernel choice and on each int8 kernel forced:
-    KVF_B200_TC=1 selects the tcgen05 kernel wherever it applies (int8 rows of
-    128 dimensions), KVF_B200_TC=0 the mma.sync kernels."""
-    env = {"auto": None, "tcgen05": "1", "mma.sync": "0"}[request.param]
-    if env is None:
-        monkeypatch.delenv("KVF_B200_TC", raising=False)
-    else:
-        monkeypatch.setenv("KVF_B200_TC", env)
+def kernel_path(request):
+    """Runs a test on the default kernel choice and on each int8 kernel forced
+    (see path_for)."""
     return request.param
+
+
+def path_for(kernel_path, fmt, d):
+    """The path argument for a kernel_path variant: "tcgen05" pins the
+    tcgen05 kernel wherever it applies (int8 rows of 128 dimensions) and the
+    mma.sync kernel elsewhere, "mma.sync" pins the mma.sync kernel."""
+    if kernel_path == "auto":
+        return "auto"
+    return "tc" if kernel_path == "tcgen05" and fmt == FMT_INT8 and d == 128 else "mma"
 
 
 def skip_if_path_irrelevant(kernel_path, fmt, d):
@@ -174,7 +181,8 @@ def test_reference_edge_plans(cuda, afix, shape_name, kernel_path):
         fname = "f16" if fmt == FMT_F16 else f"{r['fmt']}:{group}"
         place = Placement(ORD_HEAD if r["order"] == "head_major" else ORD_TOKEN, r["residency"] == "paged",
                           int(r["block_tokens"]))
-        got = run(q, K, V, fmt, group, place, int(r["splits"]), variant=_variant_id(r))
+        got = run(q, K, V, fmt, group, place, int(r["splits"]), variant=_variant_id(r),
+                  path=path_for(kernel_path, fmt, int(r["d"])))
         st = assert_close(got, afix[f"{shape_name}/{fname}"], f"{shape_name} {fname} {place.name} s={r['splits']}")
         worst[fname] = max(worst.get(fname, 0.0), st["rel_l2"])
     # the reference's kernels reported rel-L2 ~2e-7 against the same oracle
@@ -199,7 +207,7 @@ def test_config_parity(cuda, name, kernel_path):
     skip_if_path_irrelevant(kernel_path, w.fmt, w.d)
     qd, Kd, Vd, seq_lens = workloads.generate(w, cuda)
     cache = api.KVCache.from_logical(Kd, Vd, fmt=w.fmt, group=w.group, place=w.place, seq_lens=seq_lens)
-    out = api.decode(qd, cache, splits=api.suggest_splits(cache, w.H))
+    out = api.decode(qd, cache, splits=api.suggest_splits(cache, w.H), path=path_for(kernel_path, w.fmt, w.d))
     torch.cuda.synchronize()
     b_sel = None if w.B <= 8 else np.array([0, 17, 42, 63])
     sel = slice(None) if b_sel is None else torch.as_tensor(b_sel, device=cuda)
@@ -229,7 +237,7 @@ def test_ragged_and_empty_sequences(cuda, fmt, group, place, kernel_path):
     _, _, vd = O.quantize(fmt, D, group, V.reshape(-1, D))
     ref = O.attention(q, kd.reshape(K.shape), vd.reshape(V.shape), O.scale_f32(D), seq_lens=lens)
     for splits in (1, 3, 8):
-        got = run(q, K, V, fmt, group, place, splits, seq_lens=lens)
+        got = run(q, K, V, fmt, group, place, splits, seq_lens=lens, path=path_for(kernel_path, fmt, D))
         assert_close(got, ref, f"{place.name} splits={splits}")
         assert np.all(got[1] == 0.0)
 
@@ -265,7 +273,8 @@ def test_split_count_does_not_change_the_result(cuda, kernel_path):
     K = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
     V = rs.standard_normal((B, Hkv, n, D)).astype(np.float32)
     place = Placement(ORD_TOKEN, True, 64)
-    outs = [run(q, K, V, FMT_INT8, 64, place, s) for s in (1, 2, 5, 16, 64, 313)]
+    outs = [run(q, K, V, FMT_INT8, 64, place, s, path=path_for(kernel_path, FMT_INT8, D))
+            for s in (1, 2, 5, 16, 64, 313)]
     for o in outs[1:]:
         assert np.abs(o - outs[0]).max() < 1e-5
 
@@ -296,33 +305,40 @@ def test_in_kernel_split_merge_matches_two_launch_merge(cuda, fmt, group, place,
                                      fmt=fmt, group=group, place=place, seq_lens=lens)
     for splits in (2, 7, 24):
         fused_ws = api.Workspace.allocate(B, H, d, splits, cuda, fused=True)
+        path = path_for(kernel_path, fmt, d)
         for _ in range(2):
-            got = api.decode(qd, cache, workspace=fused_ws).cpu().numpy()
+            got = api.decode(qd, cache, workspace=fused_ws, path=path).cpu().numpy()
             assert_close(got, ref, f"in-kernel merge, splits={splits}")
         assert int(fused_ws.split_sem.abs().sum()) == 0
-        two = api.decode(qd, cache, workspace=api.Workspace.allocate(B, H, d, splits, cuda, fused=False))
+        two = api.decode(qd, cache, workspace=api.Workspace.allocate(B, H, d, splits, cuda, fused=False), path=path)
         assert np.abs(got - two.cpu().numpy()).max() < 1e-5, f"splits={splits}"
     assert api.device_errors() == 0
 
 
-def test_forced_tcgen05_kernel_is_the_one_that_runs(cuda, monkeypatch):
+def test_auto_path_switches_kernel_at_32_units(cuda):
+    """AUTO takes the mma.sync kernel for 8 (sequence, KV head) units and the
+    tcgen05 kernel from 32; pinned paths take theirs regardless. No
+    environment variable steers the choice."""
     rs = np.random.RandomState(17)
-    K = torch.as_tensor(rs.standard_normal((1, 8, 512, 128)).astype(np.float32), device=cuda)
-    cache = api.KVCache.from_logical(K, K, fmt=FMT_INT8, group=64, place=Placement(ORD_TOKEN, False, 0))
-    q = torch.zeros((1, 32, 128), dtype=torch.float32, device=cuda)
-    ws = api.Workspace.allocate(1, 32, 128, 4, cuda)
-    monkeypatch.setenv("KVF_B200_TC", "1")
-    assert api.describe(q, cache, ws).startswith("kernel=tcgen05")
-    monkeypatch.setenv("KVF_B200_TC", "0")
-    assert api.describe(q, cache, ws).startswith("kernel=mma.sync")
+    for B, want in ((1, "mma.sync"), (4, "tcgen05")):
+        K = torch.as_tensor(rs.standard_normal((B, 8, 512, 128)).astype(np.float32), device=cuda)
+        cache = api.KVCache.from_logical(K, K, fmt=FMT_INT8, group=64, place=Placement(ORD_TOKEN, False, 0))
+        q = torch.zeros((B, 32, 128), dtype=torch.float32, device=cuda)
+        ws = api.Workspace.allocate(B, 32, 128, 4, cuda)
+        assert api.describe(q, cache, ws).startswith(f"kernel={want}")
+        assert api.describe(q, cache, ws, path="tc").startswith("kernel=tcgen05")
+        assert api.describe(q, cache, ws, path="mma").startswith("kernel=mma.sync")
+    with pytest.raises(KvfError):
+        api.describe(q, cache, ws, path="mma", flags=api.FLAG_MERGE_KERNEL | api.FLAG_GRID_MERGE)
+    with pytest.raises(KvfError):
+        api.describe(q, cache, ws, flags=0x800)
 
 
 @pytest.mark.parametrize("place", [Placement(ORD_TOKEN, False, 0), Placement(ORD_HEAD, True, 16)],
                          ids=lambda p: p.name)
-def test_path_pinned_variants_run_their_kernel(cuda, monkeypatch, place):
+def test_path_pinned_variants_run_their_kernel(cuda, place):
     """The "_tc" / "_mma" variant ids (and api.decode(path=...)) run the named
     kernel whatever the launcher would choose, with the same results."""
-    monkeypatch.delenv("KVF_B200_TC", raising=False)
     rs = np.random.RandomState(23)
     B, H, Hkv, D, n = 2, 32, 8, 128, 700
     q = rs.standard_normal((B, H, D)).astype(np.float32)
@@ -453,7 +469,7 @@ def test_decode_from_host_rejects_pageable_buffers(cuda):
     (1, 32, 8, 3000, FMT_INT8, 64, Placement(ORD_TOKEN, False, 0)),
     (6, 16, 4, 1500, FMT_F16, 0, Placement(ORD_TOKEN, True, 16)),
 ], ids=["b1_int8_tm", "b6_f16_tm_p16"])
-def test_in_launch_grid_merge_equals_merge_kernel(cuda, monkeypatch, B, H, Hkv, n, fmt, group, place):
+def test_in_launch_grid_merge_equals_merge_kernel(cuda, B, H, Hkv, n, fmt, group, place):
     """The mma.sync kernel's split merge after a grid barrier (cooperative
     launch) gives the merge kernel's result bit for bit, launch after launch
     (its barrier counters return to zero)."""
@@ -464,12 +480,11 @@ def test_in_launch_grid_merge_equals_merge_kernel(cuda, monkeypatch, B, H, Hkv, 
     cache = api.KVCache.from_logical(K, V, fmt=fmt, group=group, place=place)
     ws = api.Workspace.allocate(B, H, 128, 7, cuda)
     outs = {}
-    for mode in ("0", "1"):
-        monkeypatch.setenv("KVF_B200_COOP", mode)
-        desc = api.describe(q, cache, ws, path="mma")
+    for mode, flags in (("0", api.FLAG_MERGE_KERNEL), ("1", api.FLAG_GRID_MERGE)):
+        desc = api.describe(q, cache, ws, path="mma", flags=flags)
         assert ("merge=in-kernel(grid)" in desc) == (mode == "1"), desc
         for _ in range(3):
-            outs[mode] = api.decode(q, cache, workspace=ws, path="mma").clone()
+            outs[mode] = api.decode(q, cache, workspace=ws, path="mma", flags=flags).clone()
         torch.cuda.synchronize()
         assert int(ws.split_sem.abs().sum()) == 0
     assert torch.equal(outs["0"], outs["1"])
@@ -480,7 +495,7 @@ def test_in_launch_grid_merge_equals_merge_kernel(cuda, monkeypatch, B, H, Hkv, 
     (FMT_F16, 0, Placement(ORD_TOKEN, True, 16)),
     (FMT_INT8, 64, Placement(ORD_HEAD, False, 0)),
 ], ids=["f16_tm_p16", "int8_hm"])
-def test_balanced_splits_on_ragged_batches(cuda, monkeypatch, fmt, group, place):
+def test_balanced_splits_on_ragged_batches(cuda, fmt, group, place):
     """Sequences of unequal length share one chunk of tokens (the mma.sync
     launch balances them over one wave of blocks): the device picks the chunk
     kvf_b200_balanced_chunk computes on the host (each sequence's partials
@@ -488,7 +503,6 @@ def test_balanced_splits_on_ragged_batches(cuda, monkeypatch, fmt, group, place)
     the oracle, and the cooperative in-launch merge, the merge kernel and a
     zero-copy Decoder step (merge kernel after a dependent launch) agree bit
     for bit."""
-    monkeypatch.setenv("KVF_B200_TC", "0")
     rs = np.random.RandomState(43)
     B, H, Hkv, D, n = 8, 32, 8, 128, 2048
     lens = np.array([2048, 0, 1, 700, 1999, 64, 1500, 333], dtype=np.int32)
@@ -501,7 +515,9 @@ def test_balanced_splits_on_ragged_batches(cuda, monkeypatch, fmt, group, place)
     qd = torch.as_tensor(q, device=cuda)
     cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
                                      fmt=fmt, group=group, place=place, seq_lens=lens)
-    S = api.suggest_splits(cache, H)
+    # The suggestion follows the AUTO kernel (tcgen05 for the int8 case); the
+    # test runs the mma.sync kernel, so it keeps a capacity of at least 8.
+    S = max(api.suggest_splits(cache, H), 8)
     bt = place.block_tokens if place.paged else 0
     assert S >= lib().kvf_b200_suggest_splits(B, H, Hkv, n, fmt, D, group, int(place.paged), bt)
     ws = api.Workspace.allocate(B, H, D, S, cuda)
@@ -514,10 +530,9 @@ def test_balanced_splits_on_ragged_batches(cuda, monkeypatch, fmt, group, place)
     assert c > 0
     sb = (lens.astype(np.int64) + c - 1) // c
     outs = {}
-    for mode in ("0", "1"):
-        monkeypatch.setenv("KVF_B200_COOP", mode)
+    for mode, flags in (("0", api.FLAG_MERGE_KERNEL), ("1", api.FLAG_GRID_MERGE)):
         ws.part_ml.fill_(float("nan"))
-        outs[mode] = api.decode(qd, cache, workspace=ws, path="mma").clone()
+        outs[mode] = api.decode(qd, cache, workspace=ws, path="mma", flags=flags).clone()
         torch.cuda.synchronize()
         written = torch.isfinite(ws.part_ml[..., 0]).cpu().numpy()  # [B][H][S]
         want = np.arange(S)[None, None, :] < sb[:, None, None]
@@ -526,23 +541,20 @@ def test_balanced_splits_on_ragged_batches(cuda, monkeypatch, fmt, group, place)
         assert int(ws.split_sem.abs().sum()) == 0
     assert torch.equal(outs["0"], outs["1"])
     assert np.all(outs["0"][1].cpu().numpy() == 0.0)
-    monkeypatch.delenv("KVF_B200_COOP")
     dec = api.Decoder(cache, H, splits=S, path="mma")
     got = dec.step(torch.as_tensor(q))
     assert torch.equal(got, outs["1"].cpu())
-    # KVF_B200_BALANCE=0: one split count for all sequences, same results.
-    monkeypatch.setenv("KVF_B200_BALANCE", "0")
-    assert "chunk=balanced" not in api.describe(qd, cache, ws, path="mma")
-    uni = api.decode(qd, cache, workspace=ws, path="mma").cpu().numpy()
+    # FLAG_NO_BALANCE: one split count for all sequences, same results.
+    assert "chunk=balanced" not in api.describe(qd, cache, ws, path="mma", flags=api.FLAG_NO_BALANCE)
+    uni = api.decode(qd, cache, workspace=ws, path="mma", flags=api.FLAG_NO_BALANCE).cpu().numpy()
     assert_close(uni, ref, "unbalanced")
     assert np.abs(uni - outs["1"].cpu().numpy()).max() < 1e-5
     assert api.device_errors() == 0
 
 
-def test_balanced_splits_fall_back_when_units_exceed_one_wave(cuda, monkeypatch):
+def test_balanced_splits_fall_back_when_units_exceed_one_wave(cuda):
     """More (sequence, head group) units than one wave of blocks: the launch
     keeps the uniform split plan, with the same results."""
-    monkeypatch.setenv("KVF_B200_TC", "0")
     rs = np.random.RandomState(44)
     B, H, Hkv, D, n = 320, 4, 4, 64, 40
     lens = rs.randint(0, n + 1, size=B).astype(np.int32)
