@@ -27,6 +27,11 @@
 //           exact product is folded into fp32 registers with the stage's
 //           rescale. The zero term sum_t p_t * vzero_t stays on the CUDA cores.
 //
+// Scores and value products are both double-buffered in tensor memory (at
+// most 256 columns, so two blocks share an SM's 512): a stage's value MMAs
+// run while the softmax warps work on the next stage, and the fold of stage
+// i - 1 follows the P' hand-over of stage i.
+//
 // Warp roles (352 threads, two blocks per SM):
 //   warps 0-7  warp w serves tensor-memory lanes 32(w%4) .. 32(w%4)+31 and half
 //              w/4 of the query heads: each thread owns one token (scores) and
@@ -34,12 +39,13 @@
 //              scores from tensor memory, runs the online softmax in the log2
 //              domain with one rescale per stage, writes P' planes, and folds
 //              each stage's value product into fp32;
-//   warps 8-9  producers (warp 8 + j takes the stages i with i % 2 == j): TMA
-//              for the K and V tiles, cp.async for the per-row quantization
-//              metadata of the same tokens (counted on the same full barrier).
-//              One warp cannot issue a stage's copies (with small pages, 16
-//              TMA boxes and 256 metadata rows) as fast as the ring drains: it
-//              shares its sub-partition's issue slots with softmax warps;
+//   warps 8-9  producers, both on every stage: warp 8 the K tile (TMA) and K
+//              metadata rows (cp.async), warp 9 the same for V, all counted
+//              on the stage's full barrier. A ring slot is held from the
+//              first copy instruction to the value MMAs, and with small pages
+//              a stage takes 16 TMA boxes and 256 metadata rows: issuing them
+//              from two warps, with every address worked out before the slot
+//              is free, keeps that time short;
 //   warp 10    MMA issuer (one thread): issues each stage's score MMAs as soon
 //              as its tiles land and each stage's value MMAs as soon as its P'
 //              planes are written, whichever comes first.
@@ -88,23 +94,27 @@ constexpr int kTcMmaWarp = 10;
 template <int GPR, int NH> struct TcMisc {
   float qinv[NH];             // 2^-eq per query head
   float qsum[NH][GPR];        // 2^-eq * sum of Qi over each group
-  float red[2][8][NH / 2 + 1];  // per-warp stage maxima (+ V-scale bits), double-buffered
+  // Stage maxima (+ V-scale bits) per half, double-buffered: high word the
+  // stage number + 1, low word the order-mapped value.
+  unsigned long long redx[2][2][NH / 2 + 1];
   float xl[8][NH / 2];        // epilogue: per-warp sums of p
   float xz[8][NH / 2][GPR];   // epilogue: per-warp sums of p * vzero
   uint32_t tmem_base;
   int abort_flag;             // set by any warp that gave up; the others stop waiting
   int last;                   // this block is the last of its (sequence, KV head)
   int slot_last[8];           // last stage whose copies went into each ring slot (-1: none)
-  // full[8], empty[8], sfull[2], sfree[2], pready, ofull, red[2 parities][2 halves], done
+  // full[8], empty[8], sfull[2], sfree[2], pready, ofull[2], red[2 parities][2 halves], done
   uint64_t bars[32];
 };
 
-// Exact int -> float for the tensor-memory sums: the integer is added to the
-// bit pattern of a power-of-two float whose ulp is 1 and the power is
-// subtracted again. s22f: |v| < 2^22 (score planes), u23f: v < 2^23 (value
-// planes).
-__device__ __forceinline__ float s22f(uint32_t v) { return __int_as_float(0x4B400000 + (int)v) - 12582912.f; }
-__device__ __forceinline__ float u23f(uint32_t v) { return __uint_as_float(0x4B000000u + v) - 8388608.f; }
+// 2^x by the hardware approximation (flush-to-zero; 2^-inf = 0). Its error,
+// a few ulp, lies far inside the output tolerance; the CUDA-core kernels keep
+// exp2f.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int GPR, int NH>
 __global__ void __launch_bounds__(kTcThreads, 2)
@@ -129,7 +139,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   volatile int *abort_flag = &ms.abort_flag;
   const uint32_t bars = ptx::smem_u32(&ms.bars[0]);
   const uint32_t bar_full = bars, bar_empty = bars + 64, bar_sfull = bars + 128, bar_sfree = bars + 144,
-                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 176, bar_done = bars + 208;
+                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 184, bar_done = bars + 216;
   const uint32_t sq = sbase + p.off_q;
 
   const int warp = threadIdx.x >> 5;
@@ -149,8 +159,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   if (tid == 0) {
     ms.abort_flag = 0;
     for (int s = 0; s < 8; ++s) ms.slot_last[s] = -1;
+    for (int e = 0; e < 2 * 2 * (NH / 2 + 1); ++e) (&ms.redx[0][0][0])[e] = 0ull;
     for (int s = 0; s < p.stages; ++s) {
-      ptx::mbar_init(bar_full + 8u * s, 33u);  // expect_tx arrival + 32 cp.async arrivals
+      ptx::mbar_init(bar_full + 8u * s, 66u);  // per producer: expect_tx arrival + 32 cp.async arrivals
       ptx::mbar_init(bar_empty + 8u * s, 1u);
     }
     for (int j = 0; j < 2; ++j) {
@@ -162,6 +173,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     }
     ptx::mbar_init(bar_pready, 8u);
     ptx::mbar_init(bar_ofull, 1u);
+    ptx::mbar_init(bar_ofull + 8u, 1u);
     ptx::mbar_init(bar_done, 1u);
     ptx::fence_barrier_init();
   }
@@ -237,11 +249,14 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 
   if (warp >= kTcProducerWarp && warp < kTcProducerWarp + kTcProducers) {
     // ----------------------------------------------------------- producers
+    // Both producers work on every stage, side by side: warp 8 copies the K
+    // tile and K metadata, warp 9 the V tile and V metadata. Block-table and
+    // metadata addresses of a stage are worked out before its slot is free,
+    // so the slot waits only for the copy instructions themselves.
     const int pw = warp - kTcProducerWarp;
-    if (lane == 0) {
-      ptx::prefetch_tmap(&tmk);
-      ptx::prefetch_tmap(&tmv);
-    }
+    const CUtensorMap *tmap = pw ? &tmv : &tmk;
+    const uint32_t *meta = reinterpret_cast<const uint32_t *>(pw ? a.v_meta : a.k_meta);
+    if (lane == 0) ptx::prefetch_tmap(tmap);
     const uint64_t pol = ptx::policy_evict_first();
     const int tbs = p.tbox_shift;
     const int bmask = (1 << p.bt_shift) - 1;
@@ -257,16 +272,10 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       if (win + 64 + lane < nblk_valid) pg_nn = __ldg(a.block_table + tab0 + win + 64 + lane);
     }
     bool ok = true;
-    for (int i = pw; i < ntiles; i += kTcProducers) {
-      const int s = i % p.stages;
-      const uint32_t phase = (uint32_t)(i / p.stages) & 1u;
-      if (i >= p.stages && !warp_wait(bar_empty + 8u * s, phase ^ 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
+    int s = 0;
+    uint32_t phase = 0;  // parity of the slot's current use
+    for (int i = 0; i < ntiles; ++i, s = (s + 1 == p.stages) ? (phase ^= 1u, 0) : s + 1) {
       const int tt = t0 + i * TB;
-      const uint32_t sk = sbase + s * p.stage_bytes;
-      const uint32_t sv = sk + TB * 128u;
       int lanepage = 0;  // page of TMA box `lane` of this stage (lanes < npg)
       if (p.paged) {
         // Box j of the stage lies in block blk0 + j (several boxes per stage
@@ -283,45 +292,47 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         const int from_nxt = __shfl_sync(0xffffffffu, pg_nxt, idx & 31);
         lanepage = idx < 32 ? from_cur : from_nxt;
       }
-      if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, 2u * TB * 128u);
-      __syncwarp();
-      if (lane < p.npg) {  // lane j issues box j of K and of V
-        const int tok = tt + (lane << tbs);
-        const int c1 = p.paged ? (tok & bmask) : tok;
-        const int c3 = p.paged ? lanepage : b;
-        const uint32_t off = (uint32_t)lane * (uint32_t)(p.tbox * 128);
-        ptx::tma_g2s_4d(sk + off, &tmk, 0, c1, h, c3, bar_full + 8u * s, pol);
-        ptx::tma_g2s_4d(sv + off, &tmv, 0, c1, h, c3, bar_full + 8u * s, pol);
-      }
-      {
-        // Metadata rows of the stage's tokens that lie inside the chunk.
-        const uint32_t *kmeta = reinterpret_cast<const uint32_t *>(a.k_meta);
-        const uint32_t *vmeta = reinterpret_cast<const uint32_t *>(a.v_meta);
-        const uint32_t smk = sv + TB * 128u;
-        const uint32_t smv = smk + p.meta_bytes;
-        for (int r = lane; r < TB; r += 32) {
-          const int tok = tt + r;
-          const int pg = p.paged ? __shfl_sync(0xffffffffu, lanepage, r >> tbs) : 0;
-          if (tok >= t1) continue;
-          long long row;
-          if (p.paged) {
-            const int tl = tok & bmask;
-            const long long base = ((long long)pg * a.Hkv) << p.bt_shift;
-            row = p.tm ? base + (long long)tl * a.Hkv + h : base + ((long long)h << p.bt_shift) + tl;
-          } else {
-            row = p.tm ? ((long long)b * a.n + tok) * a.Hkv + h : ((long long)b * a.Hkv + h) * a.n + tok;
-          }
-          const uint32_t dst = (uint32_t)(r * GPR * 4);
-          if (GPR == 1) {
-            ptx::cp_async_4(smk + dst, kmeta + row);
-            ptx::cp_async_4(smv + dst, vmeta + row);
-          } else {
-            ptx::cp_async_8(smk + dst, kmeta + row * 2);
-            ptx::cp_async_8(smv + dst, vmeta + row * 2);
-          }
+      // Metadata rows of tokens lane + 32k of the stage (null past the chunk).
+      const uint32_t *msrc[TB / 32];
+#pragma unroll
+      for (int k = 0; k < TB / 32; ++k) {
+        const int r = lane + 32 * k;
+        const int tok = tt + r;
+        const int pg = p.paged ? __shfl_sync(0xffffffffu, lanepage, r >> tbs) : 0;
+        long long row;
+        if (p.paged) {
+          const int tl = tok & bmask;
+          const long long base = ((long long)pg * a.Hkv) << p.bt_shift;
+          row = p.tm ? base + (long long)tl * a.Hkv + h : base + ((long long)h << p.bt_shift) + tl;
+        } else {
+          row = p.tm ? ((long long)b * a.n + tok) * a.Hkv + h : ((long long)b * a.Hkv + h) * a.n + tok;
         }
-        ptx::cp_async_arrive(bar_full + 8u * s);
+        msrc[k] = tok < t1 ? meta + row * GPR : nullptr;
       }
+      const int c1 = p.paged ? ((tt + (lane << tbs)) & bmask) : tt + (lane << tbs);
+      const int c3 = p.paged ? lanepage : b;
+
+      if (i >= p.stages && !warp_wait(bar_empty + 8u * s, phase ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const uint32_t sk = sbase + s * p.stage_bytes;
+      if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, TB * 128u);
+      __syncwarp();
+      if (lane < p.npg)  // lane j issues box j of the tile
+        ptx::tma_g2s_4d(sk + (uint32_t)pw * (TB * 128u) + (uint32_t)lane * (uint32_t)(p.tbox * 128), tmap, 0,
+                        c1, h, c3, bar_full + 8u * s, pol);
+      const uint32_t smeta = sk + 2u * TB * 128u + (uint32_t)pw * p.meta_bytes;
+#pragma unroll
+      for (int k = 0; k < TB / 32; ++k) {
+        if (!msrc[k]) continue;
+        const uint32_t dst = smeta + (uint32_t)((lane + 32 * k) * GPR * 4);
+        if (GPR == 1)
+          ptx::cp_async_4(dst, msrc[k]);
+        else
+          ptx::cp_async_8(dst, msrc[k]);
+      }
+      ptx::cp_async_arrive(bar_full + 8u * s);
       if (lane == 0) *reinterpret_cast<volatile int *>(&ms.slot_last[s]) = i;
       if (*abort_flag) break;
     }
@@ -377,9 +388,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
           const uint32_t sv = sk + TB * 128u;
 #pragma unroll
           for (int ks = 0; ks < TB / 32; ++ks)
-            tc::mma_i8(tbase + 2u * SC, tc::smem_desc(sv + ks * 4096u, 16384u, 1024u, tc::kSwizzle128),
+            tc::mma_i8(tbase + 2u * SC + (uint32_t)((npv & 1) * NP), tc::smem_desc(sv + ks * 4096u, 16384u, 1024u, tc::kSwizzle128),
                        tc::smem_desc(sk + ks * 512u, 128u, 2048u, tc::kSwizzleNone), ID_V, ks > 0);
-          tc::commit(bar_ofull);
+          tc::commit(bar_ofull + 8u * (npv & 1));
           tc::commit(bar_empty + 8u * (npv % p.stages));
           ++npv;
           progress = true;
@@ -447,11 +458,11 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     };
     // Folds stage k's exact value product into the fp32 accumulators.
     auto fold = [&](int k, const float (&ao)[HT]) -> bool {
-      if (!warp_wait(bar_ofull, (uint32_t)(k & 1), abort_flag)) return false;
+      if (!warp_wait(bar_ofull + 8u * (k & 1), (uint32_t)((k >> 1) & 1), abort_flag)) return false;
       tc::fence_after();
       uint32_t r[CH];
       {
-        const uint32_t ad = lane_base + 2u * SC + (uint32_t)(gd * NS + half * CH);
+        const uint32_t ad = lane_base + 2u * SC + (uint32_t)((k & 1) * NP + gd * NS + half * CH);
         if (CH == 8) {
           uint32_t t8[8];
           tc::ld8(ad, t8);
@@ -468,13 +479,17 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       tc::fence_before();
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
-        const float v = fmaf(65536.f, u23f(r[2 * HT + e]), fmaf(256.f, u23f(r[HT + e]), u23f(r[e])));
+        // Planes 0 and 1 summed exactly in 32 bits (each < 2^23), then one
+        // rounding, as fmaf(256, D1, D0) gives.
+        const uint32_t d01 = r[e] + (r[HT + e] << 8);
+        const float v = fmaf(65536.f, __uint2float_rn(r[2 * HT + e]), __uint2float_rn(d01));
         ocur[e] = fmaf(ocur[e], ao[e], v);
       }
       return true;
     };
 
-    for (int i = 0; i < ntiles; ++i) {
+    int s = 0;  // ring slot of stage i
+    for (int i = 0; i < ntiles; ++i, s = (s + 1 == p.stages) ? 0 : s + 1) {
       const int j = i & 1;
       const int tok = t0 + i * TB + row;
       const bool valid = tok < t1;
@@ -494,7 +509,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 
       // Metadata of this thread's token (rows past the chunk end hold stale
       // words and are masked).
-      const uint32_t smk = sbase + (uint32_t)(i % p.stages) * p.stage_bytes + 2u * TB * 128u;
+      const uint32_t smk = sbase + (uint32_t)s * p.stage_bytes + 2u * TB * 128u;
       const uint32_t smv = smk + p.meta_bytes;
       uint32_t kw[GPR], vw[GPR];
       if (GPR == 1) {
@@ -520,37 +535,42 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         vbits = max(vbits, vw[g] & 0x7FFFu);  // fp16 bits of a positive scale order like the values
       }
       float sc[HT];
-      float red[HT + 1];
+      float red[HT];
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
         float acc = 0.f, zq = 0.f;
 #pragma unroll
         for (int g = 0; g < GPR; ++g) {
           const uint32_t *c = sr + g * CH;
-          const float dg = fmaf(65536.f, s22f(c[2 * HT + e]), fmaf(256.f, s22f(c[HT + e]), s22f(c[e])));
+          // |D0|, |D1| < 2^22: exact 32-bit sum, then one rounding.
+          const int d01 = (int)c[e] + (int)(c[HT + e] << 8);
+          const float dg = fmaf(65536.f, __int2float_rn((int)c[2 * HT + e]), __int2float_rn(d01));
           acc = fmaf(ks[g], dg, acc);
           zq = fmaf(kz[g], qsum[e][g], zq);
         }
         sc[e] = valid ? fmaf(acc, qinv[e], zq) : -INFINITY;
         red[e] = sc[e];
       }
-      red[HT] = __uint_as_float(vbits);
       // Warp maxima in one redux.sync each: scores through an order-preserving
       // map of floats to unsigned integers (sign bit set for >= 0, all bits
-      // flipped for < 0), the V-scale bits as they are.
+      // flipped for < 0), the V-scale bits as they are. Lane e then folds
+      // value e into its half's slot with one 64-bit atomicMax whose high
+      // word is the stage number + 1, so the slot (reused every second stage)
+      // needs no clearing: a stale stage's entry always compares lower. A
+      // warp writes stage i + 2 only after all four warps of its half arrived
+      // for stage i + 1, i.e. after they read stage i.
+      uint32_t mine = 0;
 #pragma unroll
       for (int e = 0; e <= HT; ++e) {
-        uint32_t u = __float_as_uint(red[e]);
+        uint32_t u = e < HT ? __float_as_uint(red[e]) : vbits;
         if (e < HT) u = (int)u >= 0 ? (u | 0x80000000u) : ~u;
         u = __reduce_max_sync(0xffffffffu, u);
-        if (e < HT) u = (int)u < 0 ? (u & 0x7FFFFFFFu) : ~u;
-        red[e] = __uint_as_float(u);
+        if (lane == e) mine = u;
       }
-      if (lane == 0) {
-#pragma unroll
-        for (int e = 0; e <= HT; ++e) ms.red[j][warp][e] = red[e];
-        ptx::mbar_arrive(bar_red + 8u * (2 * j + half));
-      }
+      if (lane <= HT)
+        atomicMax(&ms.redx[j][half][lane], ((unsigned long long)(i + 1) << 32) | mine);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_red + 8u * (2 * j + half));
       if (!warp_wait(bar_red + 8u * (2 * j + half), (uint32_t)((i >> 1) & 1), abort_flag)) {
         ok = false;
         break;
@@ -558,14 +578,10 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       // Head and V-scale maxima over the four warps of this half (all tokens).
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
-        float v = ms.red[j][half * 4][e];
-#pragma unroll
-        for (int w = 1; w < 4; ++w) v = fmaxf(v, ms.red[j][half * 4 + w][e]);
-        red[e] = v;
+        const uint32_t u = (uint32_t)ms.redx[j][half][e];
+        red[e] = __uint_as_float((int)u < 0 ? (u & 0x7FFFFFFFu) : ~u);
       }
-      uint32_t vmax = 0;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) vmax = max(vmax, __float_as_uint(ms.red[j][half * 4 + w][HT]));
+      const uint32_t vmax = (uint32_t)ms.redx[j][half][HT];
 
       // ---- online softmax, one rescale per stage; P' as 24-bit integers
       const int ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vmax)), 24), 100), -100);
@@ -576,9 +592,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
         const float m_new = fmaxf(mrun[e], red[e]);
-        const float alpha = m_new == -INFINITY ? 1.f : exp2f(mrun[e] - m_new);
+        const float alpha = m_new == -INFINITY ? 1.f : ex2_approx(mrun[e] - m_new);
         mrun[e] = m_new;
-        const float pr = (valid && m_new != -INFINITY) ? exp2f(sc[e] - m_new) : 0.f;
+        const float pr = (valid && m_new != -INFINITY) ? ex2_approx(sc[e] - m_new) : 0.f;
         lrun[e] = fmaf(lrun[e], alpha, pr);
         aocur[e] = alpha * fratio;
 #pragma unroll
@@ -609,18 +625,11 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         }
       }
 
-      // ---- fold the previous stage's value product; after it the value
-      // accumulator in tensor memory is free for this stage's product.
-      if (i >= 1 && !fold(i - 1, aoprev)) {
-        ok = false;
-        break;
-      }
-
       // ---- P' planes into the value operand tile (MN-major, 16-byte rows of
       // 16 columns per 8-token core matrix), over the stage's K tile: the
       // score MMAs that read it completed (sfull above), and the slot is
       // handed back to the producer only after the value MMAs.
-      const uint32_t sp = sbase + (uint32_t)(i % p.stages) * p.stage_bytes;
+      const uint32_t sp = sbase + (uint32_t)s * p.stage_bytes;
       const uint32_t rowoff = (uint32_t)(row >> 3) * 128u + (uint32_t)(row & 7) * 16u;
 #pragma unroll
       for (int g = 0; g < GPR; ++g) {
@@ -637,6 +646,15 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_pready);
+
+      // ---- fold the previous stage's value product (its MMAs were issued a
+      // whole stage ago). Stage k accumulates into value buffer k % 2, and
+      // stage i + 1's MMAs, which reuse the buffer read here, are issued only
+      // after this warp's next P' arrival.
+      if (i >= 1 && !fold(i - 1, aoprev)) {
+        ok = false;
+        break;
+      }
 #pragma unroll
       for (int e = 0; e < HT; ++e) aoprev[e] = aocur[e];
     }
