@@ -15,6 +15,9 @@
                                   (bench/sweep.cu over the dispatch tables
                                   kvforge_b200.codegen emits) and the plans
                                   file the sweep test times
+  oracle/_ref/kvf                 the reference's compiler CLI (src/*.cpp,
+                                  g++), for the machine-file and planner
+                                  round trip on kvforge_b200/machines/
 
 None of the outputs is committed (.gitignore); all travel with the working
 tree to the GPU box, where the reference tree itself is absent. The
@@ -281,11 +284,30 @@ extern "C" const char *kvf_plan_{tag}() {{ return "{tag} (reference SIMT kernel)
     return built
 
 
+REF_CLI = HERE / "_ref" / "kvf"
+
+
+def build_cli(force: bool = False) -> Path | None:
+    """The reference's `kvf` compiler CLI, compiled from src/*.cpp with g++
+    (its CMake build is not used; the sources need nothing beyond the C++17
+    standard library and the reference's own include/)."""
+    if REFERENCE is None or not (REFERENCE / "src" / "main.cpp").exists():
+        return None
+    srcs = sorted((REFERENCE / "src").glob("*.cpp"))
+    hdrs = sorted((REFERENCE / "include").rglob("*.h")) + sorted((REFERENCE / "src").glob("*.h"))
+    if force or _stale(REF_CLI, srcs + hdrs):
+        REF_CLI.parent.mkdir(parents=True, exist_ok=True)
+        _run(["g++", "-std=c++17", "-O1", f"-I{REFERENCE / 'include'}", f"-I{REFERENCE / 'src'}",
+              *map(str, srcs), "-o", str(REF_CLI)])
+    return REF_CLI
+
+
 def build(force: bool = False) -> None:
     build_oracle(force)
     build_reference(force)
     build_harnesses(force)
     build_refgpu(force)
+    build_cli(force)
 
 
 if __name__ == "__main__":
