@@ -503,7 +503,7 @@ cudaError_t plan_tc(const kvf_args *a, const Shape &sh, TcLaunch &L) {
   p.off_q = (uint32_t)stages * p.stage_bytes;
   p.off_misc = p.off_q + ((qtile + 1023u) & ~1023u);
   p.smem_total = 1024u + p.off_misc + misc;
-  uint32_t cols = (uint32_t)(2 * sh.gpr * ns + 2 * np);  // two score and two value buffers
+  uint32_t cols = (uint32_t)(2 * sh.gpr * ns + np);  // two score buffers and the value accumulator
   uint32_t alloc = 32;
   while (alloc < cols) alloc <<= 1;
   p.tmem_cols = alloc;

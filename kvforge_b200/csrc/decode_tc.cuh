@@ -27,12 +27,7 @@
 //           exact product is folded into fp32 registers with the stage's
 //           rescale. The zero term sum_t p_t * vzero_t stays on the CUDA cores.
 //
-// Scores and value products are both double-buffered in tensor memory (at
-// most 256 columns, so two blocks share an SM's 512): a stage's value MMAs
-// run while the softmax warps work on the next stage, and the fold of stage
-// i - 1 follows the P' hand-over of stage i.
-//
-// Warp roles (352 threads, two blocks per SM):
+// Warp roles (384 threads, two blocks per SM):
 //   warps 0-7  warp w serves tensor-memory lanes 32(w%4) .. 32(w%4)+31 and half
 //              w/4 of the query heads: each thread owns one token (scores) and
 //              one dimension (output) for its heads. It reads the stage's
@@ -46,9 +41,11 @@
 //              a stage takes 16 TMA boxes and 256 metadata rows: issuing them
 //              from two warps, with every address worked out before the slot
 //              is free, keeps that time short;
-//   warp 10    MMA issuer (one thread): issues each stage's score MMAs as soon
-//              as its tiles land and each stage's value MMAs as soon as its P'
-//              planes are written, whichever comes first.
+//   warp 10    score-MMA issuer (one thread): a stage's score MMAs as soon as
+//              its tiles land and its score buffer is free; also allocates
+//              and frees tensor memory;
+//   warp 11    value-MMA issuer (one thread): a stage's value MMAs as soon as
+//              its P' planes are written, then hands the slot back.
 // Columns of a quantization group g are ordered g*NS + half*NS/2 + plane*NH/2 +
 // head-in-half, so each warp reads and writes only its own columns.
 // With a split-counter array (kvf_args::split_sem) the last block to finish a
@@ -85,10 +82,11 @@ struct TcPlan {
 };
 
 constexpr int kTcTokens = 128;  // tokens per stage (M of the score MMA)
-constexpr int kTcThreads = 352;     // 8 softmax warps, 2 producers, MMA issuer
+constexpr int kTcThreads = 384;     // 8 softmax warps, 2 producers, 2 MMA issuers
 constexpr int kTcProducerWarp = 8;  // and 9
 constexpr int kTcProducers = 2;
-constexpr int kTcMmaWarp = 10;
+constexpr int kTcMmaWarp = 10;      // score MMAs; allocates tensor memory
+constexpr int kTcValueWarp = 11;    // value MMAs
 
 // Scalars, exchange areas and barriers in the misc region.
 template <int GPR, int NH> struct TcMisc {
@@ -103,7 +101,7 @@ template <int GPR, int NH> struct TcMisc {
   int abort_flag;             // set by any warp that gave up; the others stop waiting
   int last;                   // this block is the last of its (sequence, KV head)
   int slot_last[8];           // last stage whose copies went into each ring slot (-1: none)
-  // full[8], empty[8], sfull[2], sfree[2], pready, ofull[2], red[2 parities][2 halves], done
+  // full[8], empty[8], sfull[2], sfree[2], pready, ofull, red[2 parities][2 halves], done[2]
   uint64_t bars[32];
 };
 
@@ -139,7 +137,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
   volatile int *abort_flag = &ms.abort_flag;
   const uint32_t bars = ptx::smem_u32(&ms.bars[0]);
   const uint32_t bar_full = bars, bar_empty = bars + 64, bar_sfull = bars + 128, bar_sfree = bars + 144,
-                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 184, bar_done = bars + 216;
+                 bar_pready = bars + 160, bar_ofull = bars + 168, bar_red = bars + 176, bar_done = bars + 208;
   const uint32_t sq = sbase + p.off_q;
 
   const int warp = threadIdx.x >> 5;
@@ -173,8 +171,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     }
     ptx::mbar_init(bar_pready, 8u);
     ptx::mbar_init(bar_ofull, 1u);
-    ptx::mbar_init(bar_ofull + 8u, 1u);
     ptx::mbar_init(bar_done, 1u);
+    ptx::mbar_init(bar_done + 8u, 1u);
     ptx::fence_barrier_init();
   }
   if (warp == kTcMmaWarp) {
@@ -352,55 +350,55 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
           atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
       }
     }
-  } else if (warp == kTcMmaWarp) {
-    // ---------------------------------------------------------- MMA issuer
+  } else if (warp == kTcMmaWarp || warp == kTcValueWarp) {
+    // --------------------------------------------------------- MMA issuers
+    // One thread each: warp 10 issues a stage's score MMAs once its tiles
+    // landed and its score buffer is free; warp 11 its value MMAs once all
+    // softmax warps handed over the stage's P' planes (which they write
+    // only after the stage's score MMAs completed).
     if (lane == 0) {
-      constexpr uint32_t ID_S = tc::idesc_i8(false, true, false, false, 128, NS);
-      constexpr uint32_t ID_V = tc::idesc_i8(false, false, true, true, 128, NP);
-      int ns = 0, npv = 0;  // next stage for the score / value MMAs
       bool ok = true;
-      uint64_t t_last = ptx::globaltimer_ns();
-      while (npv < ntiles) {
-        bool progress = false;
-        if (ns < ntiles) {
-          const int s = ns % p.stages, j = ns & 1;
-          if (ptx::mbar_test_wait(bar_full + 8u * s, (uint32_t)((ns / p.stages) & 1)) &&
-              (ns < 2 || ptx::mbar_test_wait(bar_sfree + 8u * j, (uint32_t)(((ns >> 1) - 1) & 1)))) {
-            tc::fence_after();
-            const uint32_t sk = sbase + (uint32_t)s * p.stage_bytes;
-#pragma unroll
-            for (int g = 0; g < GPR; ++g)
-#pragma unroll
-              for (int kk = 0; kk < KPG; ++kk) {
-                const int ks = g * KPG + kk;
-                tc::mma_i8(tbase + (uint32_t)(j * SC + g * NS),
-                           tc::smem_desc(sk + ks * 32u, 16u, 1024u, tc::kSwizzle128),
-                           tc::smem_desc(sq + ks * 32u, 16u, 1024u, tc::kSwizzle128), ID_S, kk > 0);
-              }
-            tc::commit(bar_sfull + 8u * j);
-            ++ns;
-            progress = true;
+      if (warp == kTcMmaWarp) {
+        constexpr uint32_t ID_S = tc::idesc_i8(false, true, false, false, 128, NS);
+        int s = 0;
+        uint32_t ph = 0;
+        for (int ns = 0; ns < ntiles; ++ns, s = (s + 1 == p.stages) ? (ph ^= 1u, 0) : s + 1) {
+          const int j = ns & 1;
+          if (!thread_wait(bar_full + 8u * s, ph, abort_flag) ||
+              (ns >= 2 && !thread_wait(bar_sfree + 8u * j, (uint32_t)(((ns >> 1) - 1) & 1), abort_flag))) {
+            ok = false;
+            break;
           }
-        }
-        if (npv < ns && ptx::mbar_test_wait(bar_pready, (uint32_t)(npv & 1))) {
           tc::fence_after();
-          const uint32_t sk = sbase + (uint32_t)(npv % p.stages) * p.stage_bytes;  // P' tile of the stage
+          const uint32_t sk = sbase + (uint32_t)s * p.stage_bytes;
+#pragma unroll
+          for (int g = 0; g < GPR; ++g)
+#pragma unroll
+            for (int kk = 0; kk < KPG; ++kk) {
+              const int ks = g * KPG + kk;
+              tc::mma_i8(tbase + (uint32_t)(j * SC + g * NS),
+                         tc::smem_desc(sk + ks * 32u, 16u, 1024u, tc::kSwizzle128),
+                         tc::smem_desc(sq + ks * 32u, 16u, 1024u, tc::kSwizzle128), ID_S, kk > 0);
+            }
+          tc::commit(bar_sfull + 8u * j);
+        }
+      } else {
+        constexpr uint32_t ID_V = tc::idesc_i8(false, false, true, true, 128, NP);
+        int s = 0;
+        for (int npv = 0; npv < ntiles; ++npv, s = (s + 1 == p.stages) ? 0 : s + 1) {
+          if (!thread_wait(bar_pready, (uint32_t)(npv & 1), abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after();
+          const uint32_t sk = sbase + (uint32_t)s * p.stage_bytes;  // P' tile of the stage
           const uint32_t sv = sk + TB * 128u;
 #pragma unroll
           for (int ks = 0; ks < TB / 32; ++ks)
-            tc::mma_i8(tbase + 2u * SC + (uint32_t)((npv & 1) * NP), tc::smem_desc(sv + ks * 4096u, 16384u, 1024u, tc::kSwizzle128),
+            tc::mma_i8(tbase + 2u * SC, tc::smem_desc(sv + ks * 4096u, 16384u, 1024u, tc::kSwizzle128),
                        tc::smem_desc(sk + ks * 512u, 128u, 2048u, tc::kSwizzleNone), ID_V, ks > 0);
-          tc::commit(bar_ofull + 8u * (npv & 1));
-          tc::commit(bar_empty + 8u * (npv % p.stages));
-          ++npv;
-          progress = true;
-        }
-        const uint64_t now = ptx::globaltimer_ns();
-        if (progress) {
-          t_last = now;
-        } else if (*abort_flag || now - t_last > 2000000000ull) {
-          ok = false;
-          break;
+          tc::commit(bar_ofull);
+          tc::commit(bar_empty + 8u * s);
         }
       }
       if (!ok) {
@@ -408,8 +406,9 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         *abort_flag = 1;
       }
       // Tensor memory is freed below only after every MMA issued here completed.
-      tc::commit(bar_done);
-      if (!ptx::mbar_wait(bar_done, 0u, 1000000000ull)) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+      const uint32_t bd = bar_done + 8u * (uint32_t)(warp - kTcMmaWarp);
+      tc::commit(bd);
+      if (!ptx::mbar_wait(bd, 0u, 1000000000ull)) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
     }
     __syncwarp();
   } else {
@@ -458,11 +457,11 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     };
     // Folds stage k's exact value product into the fp32 accumulators.
     auto fold = [&](int k, const float (&ao)[HT]) -> bool {
-      if (!warp_wait(bar_ofull + 8u * (k & 1), (uint32_t)((k >> 1) & 1), abort_flag)) return false;
+      if (!warp_wait(bar_ofull, (uint32_t)(k & 1), abort_flag)) return false;
       tc::fence_after();
       uint32_t r[CH];
       {
-        const uint32_t ad = lane_base + 2u * SC + (uint32_t)((k & 1) * NP + gd * NS + half * CH);
+        const uint32_t ad = lane_base + 2u * SC + (uint32_t)(gd * NS + half * CH);
         if (CH == 8) {
           uint32_t t8[8];
           tc::ld8(ad, t8);
@@ -571,6 +570,17 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         atomicMax(&ms.redx[j][half][lane], ((unsigned long long)(i + 1) << 32) | mine);
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_red + 8u * (2 * j + half));
+
+      // ---- while the other warps of the half deliver their maxima: fold the
+      // previous stage's value product. After it the value accumulator in
+      // tensor memory is free for this stage's product, and this warp's P'
+      // arrival for stage i (below) comes after it, so no warp can arrive
+      // for stage i + 1 before every warp's stage-i arrival has completed
+      // that phase (the value MMAs of stage i wait for it).
+      if (i >= 1 && !fold(i - 1, aoprev)) {
+        ok = false;
+        break;
+      }
       if (!warp_wait(bar_red + 8u * (2 * j + half), (uint32_t)((i >> 1) & 1), abort_flag)) {
         ok = false;
         break;
@@ -647,14 +657,6 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_pready);
 
-      // ---- fold the previous stage's value product (its MMAs were issued a
-      // whole stage ago). Stage k accumulates into value buffer k % 2, and
-      // stage i + 1's MMAs, which reuse the buffer read here, are issued only
-      // after this warp's next P' arrival.
-      if (i >= 1 && !fold(i - 1, aoprev)) {
-        ok = false;
-        break;
-      }
 #pragma unroll
       for (int e = 0; e < HT; ++e) aoprev[e] = aocur[e];
     }
