@@ -11,14 +11,13 @@ from __future__ import annotations
 
 import re
 import subprocess
-import sys
 from pathlib import Path
 
 import pytest
 
+from oracle import build as oracle_build
+
 REPO = Path(__file__).resolve().parents[1]
-sys.path.insert(0, str(REPO / "oracle"))
-import build as oracle_build  # noqa: E402
 
 MACHINE = REPO / "kvforge_b200" / "machines" / "b200-sxm.gpu"
 RESOURCES = REPO / "kvforge_b200" / "machines" / "resources_sm100.csv"
