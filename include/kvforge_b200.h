@@ -68,8 +68,11 @@ enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
  *                KV head) merges (counter word 2u of unit u); on the mma.sync
  *                path, for batches with at least two merge slices per block,
  *                a cooperative launch merges after a grid barrier (words 1
- *                and 3). NULL = the reference's two-launch scheme. Calls
- *                sharing one array must not overlap on the GPU.
+ *                and 3), and for grids of one wave with at most 64 splits
+ *                the last finishers of each (sequence, head group) g share
+ *                its merge (words 2g and 2g + 1). NULL = the reference's
+ *                two-launch scheme. Calls sharing one array must not overlap
+ *                on the GPU.
  *   lse          [B][H] fp32, optional (NULL = not written): log2 of the
  *                softmax denominator of each query head, in the same units as
  *                part_ml (max + log2(sum)); -inf for a head with no tokens.
@@ -126,9 +129,10 @@ enum { KVF_PATH_AUTO = 0, KVF_PATH_MMA = 1, KVF_PATH_TC = 2 };
 
 /* Scheduling flags, OR'ed into a path value. They choose how the mma.sync
  * launch is organised, not what it computes: every combination gives the
- * same output (the two merge schemes bit for bit).
+ * same output (the three merge schemes bit for bit).
  *   KVF_FLAG_MERGE_KERNEL  the split merge runs as its own kernel, even where
- *                          the launch would merge after a grid barrier;
+ *                          the launch would merge in-kernel (after a grid
+ *                          barrier, or by its last finishers);
  *   KVF_FLAG_GRID_MERGE    the grid-barrier merge wherever it is possible
  *                          (split_sem given, at least two (sequence, KV head)
  *                          units, every block resident), not only where it

@@ -77,6 +77,7 @@ struct Plan {
   int bt_shift;    // log2(tokens per page)
   int final_out;   // 1: write normalised out; 0: write partials
   int coop_merge;  // cooperative launch: the blocks merge the splits after a grid barrier
+  int tail_merge;  // the last finishers of each (sequence, head group) merge its splits
   int bal_gran;    // > 0: token-balanced splits (see balanced_chunk), chunk granularity
   uint32_t swz;    // swizzle mask for the K/V tiles (0x70, 0x30, 0x10)
   uint32_t box_bytes;   // one TMA box
@@ -1095,9 +1096,9 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
     if (lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
     s_abort = 1;
   }
-  // With the in-launch merge every consumer warp takes part in the barriers
+  // With an in-launch merge every consumer warp takes part in the barriers
   // below; a warp that gave up only skips its writes.
-  if (!ok && (LEAN || !p.coop_merge)) return;
+  if (!ok && !p.tail_merge && (LEAN || !p.coop_merge)) return;
   // Reduce the per-thread sums over the 8 row groups.
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -1205,6 +1206,75 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // msm is reused by the next slice
     }
   }
+  }
+
+  if (p.tail_merge) {
+    // ---- the split merge by the last finishers of this (sequence, head
+    // group). Each block takes a ticket when its partials are written; the
+    // holders of the last K tickets (K = min(splits, merge slices of the
+    // group)) wait, bounded, until every split's ticket is taken, then merge
+    // the group's (query head, 32-column) slices part, part + K, ... as
+    // merge_kernel does. The host enables this only when the grid fits in one
+    // wave, so the blocks a merger waits for are running or about to. The
+    // last merger out resets both counters for the next launch.
+    const int nthr = p.hh * 32;
+    const int S = p.splits;
+    const int nz = (D + 31) / 32;
+    const int items = p.hh * p.gq * nz;
+    const int K = min(S, items);
+    unsigned *cnt = a.split_sem + 2 * ((long long)b * p.hg + hgi);
+    __threadfence();
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    __shared__ int s_part;
+    if (threadIdx.x == 0) {
+      int part = -1;
+      if (!s_abort) {
+        const int t = (int)atomicAdd(cnt, 1u);
+        if (t >= S - K) {
+          const uint64_t tw = ptx::globaltimer_ns();
+          for (;;) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+            if ((int)v >= S) {
+              part = t - (S - K);
+              break;
+            }
+            if (ptx::globaltimer_ns() - tw > 2000000000ull) {
+              atomicOr(&g_kvfb_error, KVFB_ERR_TIMEOUT);
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+      }
+      s_part = part;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    const int part = s_part;
+    if (part >= 0) {
+      __threadfence();
+      // Scratch in the stage ring, idle now: every stage was consumed and the
+      // producer has seen all of its copies land.
+      MergeSmem &tsm = *reinterpret_cast<MergeSmem *>(smem);
+      for (int it = part; it < items; it += K) {
+        const int hq = it / nz;  // query head of the group: KV head hgi*hh + hq / gq
+        const int zc = it - hq * nz;
+        const long long head = (long long)b * a.H + (long long)hgi * p.hh * p.gq + hq;
+        const int col = zc * 32 + lane;
+        const bool colok = col < D;
+        float Mt, Lt, Ot;
+        merge_splits(a, D, head, col, colok, tsm, Mt, Lt, Ot, p.hh, S);
+        if (warp == 0) {
+          if (colok) a.out[head * D + col] = Lt > 0.f ? Ot / Lt : 0.f;
+          if (lane == 0 && zc == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // tsm is reused by the next slice
+      }
+      if (threadIdx.x == 0 && atomicAdd(cnt + 1, 1u) == (unsigned)(K - 1)) {
+        *reinterpret_cast<volatile unsigned *>(cnt) = 0u;
+        *reinterpret_cast<volatile unsigned *>(cnt + 1) = 0u;
+      }
+    }
   }
 }
 
