@@ -185,22 +185,23 @@ cudaError_t kvf_b200_merge_states(const float *o, const float *lse, int P, int r
  * decodes its own token range, and the merge kernel that combines its splits
  * also stores the result (normalised output and lse of every query head, in
  * 32-column slices) straight into the gather buffer of every rank over NVLink,
- * counts itself in on each rank with a system-scope atomic, waits (bounded)
- * until all P ranks have arrived for its slice and writes the combination of
- * the P parts (the same arithmetic as kvf_b200_merge_states) to out. One
- * decode launch plus one merge launch per step, no collective library.
- *   gather     this rank's buffer, [2][P][B*H][D+1] floats (two buffers
- *              alternate by epoch parity; a rank runs at most one step ahead)
- *   count      this rank's counters, [B*H][D/32] uint32, zero initially
- *   peer_*     the same two buffers of rank p, mapped on this GPU (p = rank
- *              included); epoch: 1, 2, 3, ... one per step. */
+ * waits (bounded) until all P parts of its slice are there and writes their
+ * combination (the same arithmetic as kvf_b200_merge_states) to out. Every
+ * value travels in one 64-bit cell together with the epoch that wrote it, so
+ * a cell that holds the current epoch is complete by itself: no fence and no
+ * counter sit between the stores and the reads. One decode launch plus one
+ * merge launch per step, no collective library.
+ *   gather       this rank's cells, [2][P][B*H][D+1] x 64 bits, zero
+ *                initially: low word the float's bits, high word the epoch
+ *                (two halves alternate by epoch parity; a rank runs at most
+ *                one step ahead)
+ *   peer_gather  the same buffer of rank p, mapped on this GPU (p = rank
+ *                included); epoch: 1, 2, 3, ... one per step. */
 typedef struct kvf_exchange {
   int P, rank, epoch;
   unsigned timeout_ms;
-  float *gather;
-  unsigned *count;
-  float *peer_gather[8];
-  unsigned *peer_count[8];
+  unsigned long long *gather;
+  unsigned long long *peer_gather[8];
 } kvf_exchange;
 
 /* kvf_b200_decode over this rank's tokens with the cross-GPU combination

@@ -858,10 +858,10 @@ extern "C" cudaError_t kvf_b200_decode_from_host(const kvf_args *a, int fmt, int
 extern "C" cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,
                                                 const kvf_exchange *x, cudaStream_t stream) {
   if (!a || !x || a->splits <= 1 || x->P < 1 || x->P > 8 || x->rank < 0 || x->rank >= x->P || !x->gather ||
-      !x->count || x->timeout_ms == 0)
+      x->timeout_ms == 0 || x->epoch < 1)
     return cudaErrorInvalidValue;
   for (int p = 0; p < x->P; ++p)
-    if (!x->peer_gather[p] || !x->peer_count[p]) return cudaErrorInvalidValue;
+    if (!x->peer_gather[p]) return cudaErrorInvalidValue;
   return decode_impl(a, fmt, d, g, ord, paged, KVF_PATH_AUTO, stream, x);
 }
 

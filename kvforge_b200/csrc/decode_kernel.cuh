@@ -1315,9 +1315,11 @@ __global__ void __launch_bounds__(kMergeWarps * 32, 2) merge_kernel(const kvf_ar
 
 // The split merge of one rank of a split-KV decode across GPUs, fused with
 // the cross-GPU exchange (see kvf_b200_decode_exchange): this rank's
-// (output slice, lse) goes into every rank's gather buffer, each rank's
-// counter for the slice is raised, and once all P parts of the slice are
-// present (bounded wait) they are combined into out.
+// (output slice, lse) goes into every rank's gather cells, and once all P
+// parts of the slice carry this step's epoch (bounded wait) they are combined
+// into out. A cell is one 64-bit store (value bits, epoch), single-copy
+// atomic over NVLink, so a reader that sees the epoch sees the value: the
+// step needs no system-scope fence and no counter.
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_exchange_kernel(const kvf_args a, int d,
                                                                          const kvf_exchange x) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1330,51 +1332,60 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_exchange_kernel(const 
   merge_splits(a, d, head, col, colok, sm, Mt, Lt, Ot);
   if ((threadIdx.x >> 5) != 0) return;
   const long long rows = (long long)a.B * a.H;
-  const int nz = gridDim.z;
-  const long long stride = d + 1;                 // floats per (rank, row): output then lse
+  const long long stride = d + 1;                 // cells per (rank, row): output then lse
   const long long par = (long long)(x.epoch & 1) * x.P;
+  const unsigned long long tag = (unsigned long long)(unsigned)x.epoch << 32;
   const float val = Lt > 0.f ? Ot / Lt : 0.f;
   const float lse = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;
-  const unsigned slot = (unsigned)(head * nz + blockIdx.z);
+  const unsigned long long cv = tag | __float_as_uint(val), cl = tag | __float_as_uint(lse);
   for (int p = 0; p < x.P; ++p) {
-    float *g = x.peer_gather[p] + ((par + x.rank) * rows + head) * stride;
-    if (colok) g[col] = val;
-    if (lane == 0) g[d] = lse;
+    unsigned long long *g = x.peer_gather[p] + ((par + x.rank) * rows + head) * stride;
+    if (colok) asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(g + col), "l"(cv) : "memory");
+    if (lane == 0) asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(g + d), "l"(cl) : "memory");
   }
-  __threadfence_system();
-  __syncwarp();
-  __shared__ int s_ok;
-  if (lane == 0) {
-    for (int p = 0; p < x.P; ++p) atomicAdd_system(x.peer_count[p] + slot, 1u);
-    // All P parts of this slice are present once the counter reaches P * epoch.
-    const unsigned want = (unsigned)x.P * (unsigned)x.epoch;
-    const uint64_t t0 = ptx::globaltimer_ns();
-    const uint64_t limit = (uint64_t)x.timeout_ms * 1000000ull;
-    int ok = 1;
-    for (;;) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(x.count + slot) : "memory");
-      if ((int)(v - want) >= 0) break;
-      if (ptx::globaltimer_ns() - t0 > limit) {
-        ok = 0;
-        break;
-      }
-      __nanosleep(32);
+  // Each lane waits for its own column of every part, lane 0 also for the
+  // lse cells; then the warp agrees.
+  const unsigned long long *base = x.gather + par * rows * stride + head * stride;
+  const uint64_t limit = (uint64_t)x.timeout_ms * 1000000ull;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  // Waits (bounded) for the cell at c to carry this step's epoch; its value.
+  auto wait_cell = [&](const unsigned long long *c, int &ok) -> float {
+    for (uint32_t it = 0; ok; ++it) {
+      unsigned long long v;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(c) : "memory");
+      if ((v >> 32) == (unsigned long long)(unsigned)x.epoch) return __uint_as_float((unsigned)v);
+      if ((it & 15u) == 15u && ptx::globaltimer_ns() - t0 > limit) ok = 0;
     }
-    if (!ok) atomicOr(&g_kvfb_error, KVFB_ERR_EXCHANGE);
-    s_ok = ok;
+    return 0.f;
+  };
+  float lp[8], op[8];
+  int ok = 1;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    lp[p] = -INFINITY;
+    op[p] = 0.f;
+    if (p < x.P) {
+      const unsigned long long *cp = base + p * rows * stride;
+      if (colok) op[p] = wait_cell(cp + col, ok);
+      if (lane == 0) lp[p] = wait_cell(cp + d, ok);
+    }
   }
-  __syncwarp();
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && lane == 0) atomicOr(&g_kvfb_error, KVFB_ERR_EXCHANGE);
   float M = -INFINITY;
-  const float *base = x.gather + par * rows * stride + head * stride;
-  for (int p = 0; p < x.P; ++p) M = fmaxf(M, __ldcg(base + p * rows * stride + d));
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    lp[p] = __shfl_sync(0xffffffffu, lp[p], 0);
+    if (p < x.P) M = fmaxf(M, lp[p]);
+  }
   float W = 0.f, O = 0.f;
-  if (M != -INFINITY && s_ok) {
-    for (int p = 0; p < x.P; ++p) {
-      const float lp = __ldcg(base + p * rows * stride + d);
-      const float w = lp == -INFINITY ? 0.f : exp2f(lp - M);
+  if (M != -INFINITY && ok) {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      if (p >= x.P) break;
+      const float w = lp[p] == -INFINITY ? 0.f : exp2f(lp[p] - M);
       W += w;
-      if (colok && w > 0.f) O = fmaf(w, __ldcg(base + p * rows * stride + col), O);
+      if (colok && w > 0.f) O = fmaf(w, op[p], O);
     }
   }
   if (colok) a.out[head * d + col] = W > 0.f ? O / W : 0.f;

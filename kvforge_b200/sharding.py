@@ -12,9 +12,9 @@ states:
 By default the exchange is fused into the decode's split merge
 (``FusedExchange``, kvf_b200_decode_exchange): the merge kernel stores each
 32-column slice of this rank's result straight into every rank's gather
-buffer over NVLink (buffers mapped through CUDA IPC), raises the slice's
-arrival counter on every rank with a system-scope atomic, waits (bounded)
-for all P parts and writes the combination, so a step is the same two
+buffer over NVLink (buffers mapped through CUDA IPC), each value in a 64-bit
+cell with the step's epoch, waits (bounded) until every part of the slice
+carries the epoch and writes the combination, so a step is the same two
 launches as on one GPU. Alternatives kept for comparison: a separate push and
 wait-and-merge pair of kernels (``PeerExchange``), or one NCCL all-gather
 plus kvf_b200_merge_states.
@@ -180,8 +180,7 @@ class KvfExchange(ctypes.Structure):
     """Mirror of kvf_exchange (kvforge_b200.h)."""
 
     _fields_ = [("P", ctypes.c_int), ("rank", ctypes.c_int), ("epoch", ctypes.c_int), ("timeout_ms", ctypes.c_uint),
-                ("gather", ctypes.c_void_p), ("count", ctypes.c_void_p),
-                ("peer_gather", ctypes.c_void_p * 8), ("peer_count", ctypes.c_void_p * 8)]
+                ("gather", ctypes.c_void_p), ("peer_gather", ctypes.c_void_p * 8)]
 
 
 def _share(L, sizes, world: int, rank: int, group):
@@ -227,9 +226,9 @@ def _unshare(L, own, opened, group):
 
 
 class FusedExchange:
-    """Buffers of the exchange fused into the split merge: gather
-    [2][P][rows][d+1] floats and counters [rows][d/32], on every rank, mapped
-    on every other rank through CUDA IPC."""
+    """Buffer of the exchange fused into the split merge: gather cells
+    [2][P][rows][d+1] x 64 bits (value, epoch), on every rank, mapped on every
+    other rank through CUDA IPC."""
 
     def __init__(self, rows: int, d: int, world: int, rank: int, group=None, timeout_ms: int = 1000):
         import torch.distributed as dist
@@ -237,15 +236,12 @@ class FusedExchange:
         if world > 8:
             raise ValueError("the fused exchange supports at most 8 ranks")
         self.L, self.group = lib(), group
-        nz = -(-d // 32)
-        self.own, peers, self.opened = _share(self.L, [2 * world * rows * (d + 1) * 4, rows * nz * 4], world, rank,
-                                              group)
+        self.own, peers, self.opened = _share(self.L, [2 * world * rows * (d + 1) * 8], world, rank, group)
         x = KvfExchange()
         x.P, x.rank, x.epoch, x.timeout_ms = world, rank, 0, timeout_ms
-        x.gather, x.count = self.own[0].value, self.own[1].value
+        x.gather = self.own[0].value
         for q in range(world):
             x.peer_gather[q] = peers[0][q]
-            x.peer_count[q] = peers[1][q]
         self.x = x
         dist.barrier(group=group)
 
