@@ -105,6 +105,12 @@ template <int GPR, int NH> struct TcMisc {
   uint64_t bars[32];
 };
 
+// Start of a running maximum: the most negative finite float, so the
+// maximum stays finite, 2^(m_old - m_new) never meets inf - inf (a finite
+// score against it gives -inf or 0 in the exponent), and a head that saw
+// only masked rows keeps it (reported as -inf).
+constexpr float kTcMinusBig = -3.402823466e38f;
+
 // 2^x by the hardware approximation (flush-to-zero; 2^-inf = 0). Its error,
 // a few ulp, lies far inside the output tolerance; the CUDA-core kernels keep
 // exp2f.
@@ -420,7 +426,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
     float mrun[HT], lrun[HT], zrun[HT][GPR], ocur[HT], aocur[HT], aoprev[HT];
 #pragma unroll
     for (int e = 0; e < HT; ++e) {
-      mrun[e] = -INFINITY;
+      mrun[e] = kTcMinusBig;
       lrun[e] = 0.f;
       ocur[e] = 0.f;
       aocur[e] = aoprev[e] = 1.f;
@@ -598,20 +604,25 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       const float fv = ev >= 0 ? exp2i(min(ev, 127)) : exp2i(max(ev, -126));
       const float fratio = exp2i(max(min(ev - ev_run, 127), -126));
       ev_run = ev;
+      // A masked row has zero scales (its metadata words were zeroed) and a
+      // score of -inf, so p = 0 and every product below is 0 without a test;
+      // the running maximum starts finite, so no exponent is ever inf - inf.
+      float vsf[GPR];
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) vsf[g] = vs[g] * fv;  // exact: fv is a power of two
       uint32_t pint[GPR][HT];
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
         const float m_new = fmaxf(mrun[e], red[e]);
-        const float alpha = m_new == -INFINITY ? 1.f : ex2_approx(mrun[e] - m_new);
+        const float alpha = ex2_approx(mrun[e] - m_new);
         mrun[e] = m_new;
-        const float pr = (valid && m_new != -INFINITY) ? ex2_approx(sc[e] - m_new) : 0.f;
+        const float pr = ex2_approx(sc[e] - m_new);
         lrun[e] = fmaf(lrun[e], alpha, pr);
         aocur[e] = alpha * fratio;
 #pragma unroll
         for (int g = 0; g < GPR; ++g) {
-          zrun[e][g] = fmaf(zrun[e][g], alpha, valid ? pr * vz[g] : 0.f);
-          const float pv = valid ? pr * vs[g] * fv : 0.f;
-          pint[g][e] = min(__float2uint_rn(pv), 0xFFFFFFu);
+          zrun[e][g] = fmaf(zrun[e][g], alpha, pr * vz[g]);
+          pint[g][e] = min(__float2uint_rn(pr * vsf[g]), 0xFFFFFFu);
         }
       }
       // Byte planes: column plane*HT + head of this half.
@@ -703,7 +714,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         } else {
           a.part_o[(head * p.splits + split) * D + row] = val;
           if (row == 0) {
-            a.part_ml[(head * p.splits + split) * 2] = mrun[e];
+            a.part_ml[(head * p.splits + split) * 2] = mrun[e] == kTcMinusBig ? -INFINITY : mrun[e];
             a.part_ml[(head * p.splits + split) * 2 + 1] = L;
           }
         }
