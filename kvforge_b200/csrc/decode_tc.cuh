@@ -22,8 +22,8 @@
 //   values  O^T[128 dims x cols] = V codes (u8, read MN-major from the same
 //           tile) * P' planes (u8, written over the stage's K tile, which is
 //           dead once the score MMAs completed), where P'_t = rint(p_t * vscale_t * 2^ev) is a
-//           24-bit integer per (token, head, group) split into three byte planes;
-//           ev puts the stage's largest V scale in [2^23, 2^24). Each stage's
+//           23-bit integer per (token, head, group) split into byte planes;
+//           ev puts the stage's largest V scale in [2^22, 2^23). Each stage's
 //           exact product is folded into fp32 registers with the stage's
 //           rescale. The zero term sum_t p_t * vzero_t stays on the CUDA cores.
 //
@@ -46,8 +46,11 @@
 //              and frees tensor memory;
 //   warp 11    value-MMA issuer (one thread): a stage's value MMAs as soon as
 //              its P' planes are written, then hands the slot back.
-// Columns of a quantization group g are ordered g*NS + half*NS/2 + plane*NH/2 +
-// head-in-half, so each warp reads and writes only its own columns.
+// Score columns of a quantization group g are ordered g*NS + half*NS/2 +
+// plane*NH/2 + head-in-half, value (P') columns g*NS + half*NS/2 +
+// 4*head-in-half + plane (planes 0-2 of P'; the fourth byte of a head's word
+// is not part of it and its column is never read), so each warp reads and
+// writes only its own columns.
 // With a split-counter array (kvf_args::split_sem) the last block to finish a
 // (sequence, KV head) merges that head's split partials itself
 // (decode_merge, runtime/kvf_kernels.cuh:288-306), so no second kernel runs.
@@ -440,7 +443,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 #pragma unroll
       for (int g = 0; g < GPR; ++g) qsum[e][g] = ms.qsum[half * HT + e][g];
     }
-    int ev_run = 23;
+    int ev_run = 22;
     bool ok = true;
 
     // Loads this half's CH columns of each group from tensor memory.
@@ -486,8 +489,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       for (int e = 0; e < HT; ++e) {
         // Planes 0 and 1 summed exactly in 32 bits (each < 2^23), then one
         // rounding, as fmaf(256, D1, D0) gives.
-        const uint32_t d01 = r[e] + (r[HT + e] << 8);
-        const float v = fmaf(65536.f, __uint2float_rn(r[2 * HT + e]), __uint2float_rn(d01));
+        const uint32_t d01 = r[4 * e] + (r[4 * e + 1] << 8);
+        const float v = fmaf(65536.f, __uint2float_rn(r[4 * e + 2]), __uint2float_rn(d01));
         ocur[e] = fmaf(ocur[e], ao[e], v);
       }
       return true;
@@ -599,8 +602,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       }
       const uint32_t vmax = (uint32_t)ms.redx[j][half][HT];
 
-      // ---- online softmax, one rescale per stage; P' as 24-bit integers
-      const int ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vmax)), 24), 100), -100);
+      // ---- online softmax, one rescale per stage; P' as 23-bit integers
+      const int ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vmax)), 23), 100), -100);
       const float fv = ev >= 0 ? exp2i(min(ev, 127)) : exp2i(max(ev, -126));
       const float fratio = exp2i(max(min(ev - ev_run, 127), -126));
       ev_run = ev;
@@ -610,7 +613,15 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       float vsf[GPR];
 #pragma unroll
       for (int g = 0; g < GPR; ++g) vsf[g] = vs[g] * fv;  // exact: fv is a power of two
-      uint32_t pint[GPR][HT];
+      // P' = rint(p * vscale * 2^ev) < 2^23 (+1 at most, from the rounding of
+      // p <= 1): the magic 2^23 added inside the FMA rounds the product to an
+      // integer (floats in [2^23, 2^24) have a unit ulp), and the float's
+      // three low bytes are that integer (2^23 itself becomes 2^24, whose low
+      // bytes read 0x800000 all the same). The fourth byte (0x4B, exponent
+      // bits) goes to the fourth column of the head, which the fold ignores.
+      uint32_t pint[GPR][4];
+#pragma unroll
+      for (int g = 0; g < GPR; ++g) pint[g][2 % HT] = pint[g][3 % HT] = 0u;
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
         const float m_new = fmaxf(mrun[e], red[e]);
@@ -622,27 +633,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 #pragma unroll
         for (int g = 0; g < GPR; ++g) {
           zrun[e][g] = fmaf(zrun[e][g], alpha, pr * vz[g]);
-          pint[g][e] = min(__float2uint_rn(pr * vsf[g]), 0xFFFFFFu);
-        }
-      }
-      // Byte planes: column plane*HT + head of this half.
-      uint32_t pw[GPR][4];
-#pragma unroll
-      for (int g = 0; g < GPR; ++g) {
-        if (HT == 2) {
-          const uint32_t p0 = pint[g][0], p1 = pint[g][HT - 1];
-          pw[g][0] = ptx::prmt(ptx::prmt(p0, p1, 0x40u), ptx::prmt(p0, p1, 0x51u), 0x5410u);
-          pw[g][1] = ptx::prmt(p0, p1, 0x3362u);
-          pw[g][2] = pw[g][3] = 0u;
-        } else {
-#pragma unroll
-          for (int pl = 0; pl < 3; ++pl) {
-            const uint32_t sel = (uint32_t)pl | ((uint32_t)(4 + pl) << 4);
-            const uint32_t lo = ptx::prmt(pint[g][0], pint[g][1 % HT], sel);
-            const uint32_t hi = ptx::prmt(pint[g][2 % HT], pint[g][3 % HT], sel);
-            pw[g][pl] = ptx::prmt(lo, hi, 0x5410u);
-          }
-          pw[g][3] = 0u;
+          pint[g][e] = __float_as_uint(fmaf(pr, vsf[g], 8388608.f));
         }
       }
 
@@ -656,11 +647,11 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       for (int g = 0; g < GPR; ++g) {
         if (CH == 8) {
           asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(sp + (uint32_t)g * 2048u + rowoff + 8u * half),
-                       "r"(pw[g][0]), "r"(pw[g][1])
+                       "r"(pint[g][0]), "r"(pint[g][1])
                        : "memory");
         } else {
           asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(sp + (uint32_t)(2 * g + half) * 2048u + rowoff),
-                       "r"(pw[g][0]), "r"(pw[g][1]), "r"(pw[g][2]), "r"(pw[g][3])
+                       "r"(pint[g][0]), "r"(pint[g][1]), "r"(pint[g][2]), "r"(pint[g][3])
                        : "memory");
         }
       }
