@@ -559,21 +559,24 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         sc[e] = valid ? fmaf(acc, qinv[e], zq) : -INFINITY;
         red[e] = sc[e];
       }
-      // Warp maxima in one redux.sync each: scores through an order-preserving
-      // map of floats to unsigned integers (sign bit set for >= 0, all bits
-      // flipped for < 0), the V-scale bits as they are. Lane e then folds
-      // value e into its half's slot with one 64-bit atomicMax whose high
-      // word is the stage number + 1, so the slot (reused every second stage)
-      // needs no clearing: a stale stage's entry always compares lower. A
-      // warp writes stage i + 2 only after all four warps of its half arrived
-      // for stage i + 1, i.e. after they read stage i.
-      uint32_t mine = 0;
+      // Warp maxima in one redux.sync each (scores as floats, the V-scale
+      // bits as integers). Lane e then folds value e into its half's slot
+      // with one 64-bit atomicMax whose high word is the stage number + 1, so
+      // the slot (reused every second stage) needs no clearing: a stale
+      // stage's entry always compares lower; a score goes in through an
+      // order-preserving map of floats to unsigned integers (sign bit set for
+      // >= 0, all bits flipped for < 0). A warp writes stage i + 2 only after
+      // all four warps of its half arrived for stage i + 1, i.e. after they
+      // read stage i.
+      uint32_t mine = __reduce_max_sync(0xffffffffu, vbits);
 #pragma unroll
-      for (int e = 0; e <= HT; ++e) {
-        uint32_t u = e < HT ? __float_as_uint(red[e]) : vbits;
-        if (e < HT) u = (int)u >= 0 ? (u | 0x80000000u) : ~u;
-        u = __reduce_max_sync(0xffffffffu, u);
-        if (lane == e) mine = u;
+      for (int e = 0; e < HT; ++e) {
+        float v;
+        asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(v) : "f"(red[e]));
+        if (lane == e) {
+          const uint32_t u = __float_as_uint(v);
+          mine = (int)u >= 0 ? (u | 0x80000000u) : ~u;
+        }
       }
       if (lane <= HT)
         atomicMax(&ms.redx[j][half][lane], ((unsigned long long)(i + 1) << 32) | mine);
