@@ -108,6 +108,36 @@ template <int GPR, int NH> struct TcMisc {
   uint64_t bars[32];
 };
 
+// Two fp32 operations in one instruction (sm_100a packed f32x2), each lane
+// rounded to nearest exactly as fmaf / __fmul_rn / __fsub_rn round.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
 // Start of a running maximum: the most negative finite float, so the
 // maximum stays finite, 2^(m_old - m_new) never meets inf - inf (a finite
 // score against it gives -inf or 0 in the exponent), and a head that saw
@@ -485,13 +515,17 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       }
       tc::wait_ld();
       tc::fence_before();
+      // Heads in pairs: planes 0 and 1 summed exactly in 32 bits (each
+      // < 2^23), then one rounding, as fmaf(256, D1, D0) gives.
 #pragma unroll
-      for (int e = 0; e < HT; ++e) {
-        // Planes 0 and 1 summed exactly in 32 bits (each < 2^23), then one
-        // rounding, as fmaf(256, D1, D0) gives.
-        const uint32_t d01 = r[4 * e] + (r[4 * e + 1] << 8);
-        const float v = fmaf(65536.f, __uint2float_rn(r[4 * e + 2]), __uint2float_rn(d01));
-        ocur[e] = fmaf(ocur[e], ao[e], v);
+      for (int e = 0; e < HT; e += 2) {
+        const uint32_t d0 = r[4 * e] + (r[4 * e + 1] << 8), d1 = r[4 * e + 4] + (r[4 * e + 5] << 8);
+        const float2 v = fma2(make_float2(65536.f, 65536.f),
+                              make_float2(__uint2float_rn(r[4 * e + 2]), __uint2float_rn(r[4 * e + 6])),
+                              make_float2(__uint2float_rn(d0), __uint2float_rn(d1)));
+        const float2 o = fma2(make_float2(ocur[e], ocur[e + 1]), make_float2(ao[e], ao[e + 1]), v);
+        ocur[e] = o.x;
+        ocur[e + 1] = o.y;
       }
       return true;
     };
@@ -544,20 +578,26 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       }
       float sc[HT];
       float red[HT];
+      // Heads in pairs (packed f32x2 arithmetic).
 #pragma unroll
-      for (int e = 0; e < HT; ++e) {
-        float acc = 0.f, zq = 0.f;
+      for (int e = 0; e < HT; e += 2) {
+        float2 acc = make_float2(0.f, 0.f), zq = make_float2(0.f, 0.f);
 #pragma unroll
         for (int g = 0; g < GPR; ++g) {
           const uint32_t *c = sr + g * CH;
-          // |D0|, |D1| < 2^22: exact 32-bit sum, then one rounding.
-          const int d01 = (int)c[e] + (int)(c[HT + e] << 8);
-          const float dg = fmaf(65536.f, __int2float_rn((int)c[2 * HT + e]), __int2float_rn(d01));
-          acc = fmaf(ks[g], dg, acc);
-          zq = fmaf(kz[g], qsum[e][g], zq);
+          // |D0|, |D1| < 2^22: exact 32-bit sums, then one rounding.
+          const int d0 = (int)c[e] + (int)(c[HT + e] << 8), d1 = (int)c[e + 1] + (int)(c[HT + e + 1] << 8);
+          const float2 dg = fma2(make_float2(65536.f, 65536.f),
+                                 make_float2(__int2float_rn((int)c[2 * HT + e]), __int2float_rn((int)c[2 * HT + e + 1])),
+                                 make_float2(__int2float_rn(d0), __int2float_rn(d1)));
+          acc = fma2(make_float2(ks[g], ks[g]), dg, acc);
+          zq = fma2(make_float2(kz[g], kz[g]), make_float2(qsum[e][g], qsum[e + 1][g]), zq);
         }
-        sc[e] = valid ? fmaf(acc, qinv[e], zq) : -INFINITY;
+        const float2 s2 = fma2(acc, make_float2(qinv[e], qinv[e + 1]), zq);
+        sc[e] = valid ? s2.x : -INFINITY;
+        sc[e + 1] = valid ? s2.y : -INFINITY;
         red[e] = sc[e];
+        red[e + 1] = sc[e + 1];
       }
       // Warp maxima in one redux.sync each (scores as floats, the V-scale
       // bits as integers). Lane e then folds value e into its half's slot
@@ -626,17 +666,28 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 #pragma unroll
       for (int g = 0; g < GPR; ++g) pint[g][2 % HT] = pint[g][3 % HT] = 0u;
 #pragma unroll
-      for (int e = 0; e < HT; ++e) {
-        const float m_new = fmaxf(mrun[e], red[e]);
-        const float alpha = ex2_approx(mrun[e] - m_new);
-        mrun[e] = m_new;
-        const float pr = ex2_approx(sc[e] - m_new);
-        lrun[e] = fmaf(lrun[e], alpha, pr);
-        aocur[e] = alpha * fratio;
+      for (int e = 0; e < HT; e += 2) {
+        const float2 mo = make_float2(mrun[e], mrun[e + 1]);
+        const float2 mn = make_float2(fmaxf(mo.x, red[e]), fmaxf(mo.y, red[e + 1]));
+        const float2 da = sub2(mo, mn), ds = sub2(make_float2(sc[e], sc[e + 1]), mn);
+        const float2 alpha = make_float2(ex2_approx(da.x), ex2_approx(da.y));
+        const float2 pr = make_float2(ex2_approx(ds.x), ex2_approx(ds.y));
+        mrun[e] = mn.x;
+        mrun[e + 1] = mn.y;
+        const float2 l2 = fma2(make_float2(lrun[e], lrun[e + 1]), alpha, pr);
+        lrun[e] = l2.x;
+        lrun[e + 1] = l2.y;
+        const float2 a2 = mul2(alpha, make_float2(fratio, fratio));
+        aocur[e] = a2.x;
+        aocur[e + 1] = a2.y;
 #pragma unroll
         for (int g = 0; g < GPR; ++g) {
-          zrun[e][g] = fmaf(zrun[e][g], alpha, pr * vz[g]);
-          pint[g][e] = __float_as_uint(fmaf(pr, vsf[g], 8388608.f));
+          const float2 z2 = fma2(make_float2(zrun[e][g], zrun[e + 1][g]), alpha, mul2(pr, make_float2(vz[g], vz[g])));
+          zrun[e][g] = z2.x;
+          zrun[e + 1][g] = z2.y;
+          const float2 p2 = fma2(pr, make_float2(vsf[g], vsf[g]), make_float2(8388608.f, 8388608.f));
+          pint[g][e] = __float_as_uint(p2.x);
+          pint[g][e + 1] = __float_as_uint(p2.y);
         }
       }
 
