@@ -316,6 +316,54 @@ __device__ __forceinline__ bool thread_wait(uint32_t bar, uint32_t parity, volat
   }
 }
 
+// Two fp32 operations in one instruction (sm_100a packed f32x2), each lane
+// rounded to nearest exactly as fmaf / __fmul_rn / __fsub_rn round.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+// 2^x by the hardware approximation (flush-to-zero; 2^-inf = 0). Its error,
+// a few ulp, lies far inside the output tolerance; it replaces exp2f in the
+// softmax of both decode kernels.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 2^e as a float, for e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
@@ -879,39 +927,43 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
               }
             }
           }
-          // Combine parts and groups for rows g8 and g8 + 8 of the m-tile:
+          // Combine parts and groups for rows g8 and g8 + 8 of the m-tile, the
+          // two rows as one packed f32x2 pair:
           // s = 2^-eq * sum_g scale_g * dot_g + sum_g zero'_g * qsum_g.
+          float2 ksc[NG], kz[NG];
+          if (GPR > 0) {
+            uint32_t w0[NG], w1[NG];
+            load_meta(smk, mt, 0, w0);
+            load_meta(smk, mt, 1, w1);
 #pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            float ksc[NG], kz[NG];
+            for (int gi = 0; gi < NG; ++gi) {
+              const float2 f0 = meta_sz(w0[gi]), f1 = meta_sz(w1[gi]);
+              ksc[gi] = make_float2(f0.x, f1.x);
+              kz[gi] = fma2(make_float2(CENTRE, CENTRE), ksc[gi], make_float2(f0.y, f1.y));
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            float2 v;
             if (GPR > 0) {
-              uint32_t w[NG];
-              load_meta(smk, mt, rr, w);
+              float2 dsum = make_float2(0.f, 0.f), zq = make_float2(0.f, 0.f);
 #pragma unroll
               for (int gi = 0; gi < NG; ++gi) {
-                const float2 f = meta_sz(w[gi]);
-                ksc[gi] = f.x;
-                kz[gi] = fmaf(CENTRE, f.x, f.y);
+                const float2 d = add2(make_float2(acc[gi][nt][0], acc[gi][nt][2]),
+                                      make_float2(acc[gi][nt][1], acc[gi][nt][3]));
+                dsum = fma2(ksc[gi], d, dsum);
+                zq = fma2(kz[gi], make_float2(qs[gi][nt], qs[gi][nt]), zq);
               }
+              v = fma2(dsum, make_float2(qinv[nt], qinv[nt]), zq);
+            } else {
+              v = mul2(add2(make_float2(acc[0][nt][0], acc[0][nt][2]), make_float2(acc[0][nt][1], acc[0][nt][3])),
+                       make_float2(qinv[nt], qinv[nt]));
             }
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              float v;
-              if (GPR > 0) {
-                float dsum = 0.f, zq = 0.f;
-#pragma unroll
-                for (int gi = 0; gi < NG; ++gi) {
-                  dsum = fmaf(ksc[gi], acc[gi][nt][2 * rr] + acc[gi][nt][2 * rr + 1], dsum);
-                  zq = fmaf(kz[gi], qs[gi][nt], zq);
-                }
-                v = fmaf(dsum, qinv[nt], zq);
-              } else {
-                v = (acc[0][nt][2 * rr] + acc[0][nt][2 * rr + 1]) * qinv[nt];
-              }
-              if (!FULL && mt * 16 + g8 + rr * 8 >= vt) v = -INFINITY;
-              sc[mt][nt][rr] = v;
-              tmax[nt] = fmaxf(tmax[nt], v);
-            }
+            if (!FULL && mt * 16 + g8 >= vt) v.x = -INFINITY;
+            if (!FULL && mt * 16 + g8 + 8 >= vt) v.y = -INFINITY;
+            sc[mt][nt][0] = v.x;
+            sc[mt][nt][1] = v.y;
+            tmax[nt] = fmaxf(tmax[nt], fmaxf(v.x, v.y));
           }
         }
       }
@@ -949,7 +1001,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m_run[nt], mx);
-        const float alpha = exp2f(m_run[nt] - m_new);  // 0 on the first stage
+        const float alpha = ex2_approx(m_run[nt] - m_new);  // 0 on the first stage
         m_run[nt] = m_new;
         l_run[nt] *= alpha;
 #pragma unroll
@@ -964,44 +1016,47 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         if (FULL || mt < nmt) {
-          float pr[NT][2];
+          // Probabilities of this thread's two tokens (rows g8, g8 + 8) as a
+          // packed pair; 0 for masked rows.
+          float2 pr[NT];
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
+          for (int nt = 0; nt < NT; ++nt) {
+            const float2 d = sub2(make_float2(sc[mt][nt][0], sc[mt][nt][1]), make_float2(m_run[nt], m_run[nt]));
+            pr[nt] = make_float2(ex2_approx(d.x), ex2_approx(d.y));
+            l_run[nt] += pr[nt].x;
+            l_run[nt] += pr[nt].y;
+          }
+          // Value scale (times 2^ev) and centred zero of the two tokens; 0 for
+          // masked rows so stale bits never leak in.
+          float2 vsc[NG], vz[NG];
+          const bool valid0 = FULL || mt * 16 + g8 < vt, valid1 = FULL || mt * 16 + g8 + 8 < vt;
+          if (GPR > 0) {
+            uint32_t w0[NG], w1[NG];
+            load_meta(smv, mt, 0, w0);
+            load_meta(smv, mt, 1, w1);
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              const float pv = exp2f(sc[mt][nt][rr] - m_run[nt]);  // 0 for masked rows
-              pr[nt][rr] = pv;
-              l_run[nt] += pv;
+            for (int gi = 0; gi < NG; ++gi) {
+              const float2 f0 = meta_sz(w0[gi]), f1 = meta_sz(w1[gi]);
+              const float2 sv = make_float2(f0.x, f1.x);
+              vsc[gi] = mul2(sv, make_float2(fv, fv));
+              vz[gi] = fma2(make_float2(CENTRE, CENTRE), sv, make_float2(f0.y, f1.y));
+              if (!valid0) vsc[gi].x = vz[gi].x = 0.f;
+              if (!valid1) vsc[gi].y = vz[gi].y = 0.f;
             }
-          // Value scale (times 2^ev) and centred zero of this thread's two
-          // tokens; 0 for masked rows so stale bits never leak in.
-          float vsc[NG][2], vz[NG][2];
-#pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            const bool valid = FULL || mt * 16 + g8 + rr * 8 < vt;
-            if (GPR > 0) {
-              uint32_t w[NG];
-              load_meta(smv, mt, rr, w);
-#pragma unroll
-              for (int gi = 0; gi < NG; ++gi) {
-                const float2 f = meta_sz(w[gi]);
-                vsc[gi][rr] = valid ? f.x * fv : 0.f;
-                vz[gi][rr] = valid ? fmaf(CENTRE, f.x, f.y) : 0.f;
-              }
-            } else {
-              vsc[0][rr] = valid ? fv : 0.f;
-              vz[0][rr] = 0.f;
-            }
+          } else {
+            vsc[0] = make_float2(valid0 ? fv : 0.f, valid1 ? fv : 0.f);
+            vz[0] = make_float2(0.f, 0.f);
           }
 #pragma unroll
           for (int gi = 0; gi < NG; ++gi)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const uint32_t w0 = split_hi_lo(pr[nt][0] * vsc[gi][0]);
-              const uint32_t w1 = split_hi_lo(pr[nt][1] * vsc[gi][1]);
+              const float2 pp = mul2(pr[nt], vsc[gi]);
+              const uint32_t w0 = split_hi_lo(pp.x);
+              const uint32_t w1 = split_hi_lo(pp.y);
               if (GPR > 0) {
-                z_run[gi][nt] = fmaf(pr[nt][0], vz[gi][0], z_run[gi][nt]);
-                z_run[gi][nt] = fmaf(pr[nt][1], vz[gi][1], z_run[gi][nt]);
+                z_run[gi][nt] = fmaf(pr[nt].x, vz[gi].x, z_run[gi][nt]);
+                z_run[gi][nt] = fmaf(pr[nt].y, vz[gi].y, z_run[gi][nt]);
               }
               stsm_x2_t(pscr + (uint32_t)((gi * NT + nt) * 384 + st_row * 48 + st_mat * 16), w0, w1);
             }
@@ -1074,8 +1129,12 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              o[DT * xi + k][nt][e] = fmaf(o[DT * xi + k][nt][e], ao[nt], tacc[k][nt][e]);
+            for (int e = 0; e < 4; e += 2) {
+              const float2 r = fma2(make_float2(o[DT * xi + k][nt][e], o[DT * xi + k][nt][e + 1]),
+                                    make_float2(ao[nt], ao[nt]), make_float2(tacc[k][nt][e], tacc[k][nt][e + 1]));
+              o[DT * xi + k][nt][e] = r.x;
+              o[DT * xi + k][nt][e + 1] = r.y;
+            }
       }
     };
     if (vt == TB)

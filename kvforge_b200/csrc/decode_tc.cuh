@@ -108,50 +108,11 @@ template <int GPR, int NH> struct TcMisc {
   uint64_t bars[32];
 };
 
-// Two fp32 operations in one instruction (sm_100a packed f32x2), each lane
-// rounded to nearest exactly as fmaf / __fmul_rn / __fsub_rn round.
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return r;
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-  float2 r;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
-}
-
 // Start of a running maximum: the most negative finite float, so the
 // maximum stays finite, 2^(m_old - m_new) never meets inf - inf (a finite
 // score against it gives -inf or 0 in the exponent), and a head that saw
 // only masked rows keeps it (reported as -inf).
 constexpr float kTcMinusBig = -3.402823466e38f;
-
-// 2^x by the hardware approximation (flush-to-zero; 2^-inf = 0). Its error,
-// a few ulp, lies far inside the output tolerance; the CUDA-core kernels keep
-// exp2f.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 template <int GPR, int NH>
 __global__ void __launch_bounds__(kTcThreads, 2)
