@@ -279,6 +279,43 @@ def test_split_count_does_not_change_the_result(cuda, kernel_path):
         assert np.abs(o - outs[0]).max() < 1e-5
 
 
+@pytest.mark.parametrize("fmt,group,place,d,gq,n,splits", [
+    (FMT_F16, 0, Placement(ORD_HEAD, False, 0), 128, 1, 4096, 37),      # mha: 8 head groups x 37
+    (FMT_INT8, 64, Placement(ORD_TOKEN, False, 0), 128, 4, 9000, 48),   # gqa int8: 2 head groups x 48
+    (FMT_INT4, 32, Placement(ORD_HEAD, False, 0), 128, 4, 5000, 48),    # gqa int4, some splits empty
+    (FMT_F16, 0, Placement(ORD_TOKEN, False, 0), 64, 2, 3000, 64),      # d=64, the most splits it takes
+])
+def test_tail_merge_matches_the_merge_kernel(cuda, fmt, group, place, d, gq, n, splits):
+    """A single sequence on the mma.sync kernel with split counters and at
+    most 64 splits in one wave: the last finishers of each head group merge
+    the splits inside the launch. The result equals the separate merge
+    kernel's bit for bit (the same merge arithmetic), matches the oracle, and
+    the counters are back at zero after every call."""
+    rs = np.random.RandomState(21)
+    B, Hkv = 1, 8
+    H = Hkv * gq
+    q = rs.standard_normal((B, H, d)).astype(np.float32)
+    K = rs.standard_normal((B, Hkv, n, d)).astype(np.float32)
+    V = rs.standard_normal((B, Hkv, n, d)).astype(np.float32)
+    _, _, kq = O.quantize(fmt, d, group, K.reshape(-1, d))
+    _, _, vq = O.quantize(fmt, d, group, V.reshape(-1, d))
+    ref = O.attention(q, kq.reshape(K.shape), vq.reshape(V.shape), O.scale_f32(d))
+    qd = torch.as_tensor(q, device=cuda)
+    cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                     fmt=fmt, group=group, place=place)
+    ws = api.Workspace.allocate(B, H, d, splits, cuda, fused=True)
+    assert "merge=in-kernel(tail)" in api.describe(qd, cache, ws, path="mma")
+    outs = []
+    for _ in range(3):
+        outs.append(api.decode(qd, cache, workspace=ws, path="mma").cpu().numpy())
+        assert int(ws.split_sem.abs().sum()) == 0
+    two = api.decode(qd, cache, workspace=ws, path="mma", flags=api.FLAG_MERGE_KERNEL).cpu().numpy()
+    for o in outs:
+        assert np.array_equal(o, two)
+    assert_close(outs[0], ref, f"tail merge fmt={fmt} d={d} splits={splits}")
+    assert api.device_errors() == 0
+
+
 @pytest.mark.parametrize("fmt,group,place,d,gq", [
     (FMT_INT8, 64, Placement(ORD_TOKEN, True, 16), 128, 4),
     (FMT_INT8, 128, Placement(ORD_HEAD, False, 0), 128, 8),
