@@ -297,7 +297,8 @@ cudaError_t kvf_b200_describe_path(const kvf_args *a, int fmt, int d, int ord, i
  * shared-memory barrier wait in a decode kernel ran out of time (the kernel
  * abandoned the step and its output is not valid). Bit 1: a cross-GPU wait
  * of kvf_b200_decode_exchange ran out of time (the affected output slices are
- * zero). 0 = no error. This call synchronises with the device. */
+ * zero). Bit 2: kvf_b200_append met a token outside the cache (not written).
+ * 0 = no error. This call synchronises with the device. */
 unsigned kvf_b200_device_errors(void);
 
 /* Quantizes `rows` logical rows of d fp32 channels (device memory) into the
@@ -307,6 +308,24 @@ unsigned kvf_b200_device_errors(void);
  * words (scale | zero << 16, fp16). f16 ignores group and meta. */
 cudaError_t kvf_b200_quantize(int fmt, int d, int group, const float *x, long long rows,
                               unsigned char *data, void *meta, cudaStream_t stream);
+
+/* Appends t_new tokens to every sequence of a cache on the device: the new
+ * rows k_new, v_new (fp32 [B][Hkv][t_new][d], device memory, logical order)
+ * are quantized exactly as kvf_b200_quantize does (kvf::quantize,
+ * runtime/kvf_host.h:72-120) and their codes and (scale, zero) words written
+ * at the physical rows of tokens pos[b] .. pos[b] + t_new - 1 in the cache
+ * `a` describes (row formula of runtime/kvf_kernels.cuh:51-64 and
+ * kvf_host.h:124-135 for `ord` and `paged`; read: k, v, k_meta, v_meta,
+ * block_table, max_blocks, block_shift, group_shift, B, Hkv, n; the cache
+ * buffers are written through). pos: device int[B], the first new token of
+ * each sequence, usually its length so far; the caller then raises its
+ * seq_lens by t_new. For a paged cache the block table must already map every
+ * block the new tokens fall in. A token at or past n, or in a block past
+ * max_blocks, is skipped and sets bit 2 of kvf_b200_device_errors(). No
+ * reference counterpart: the reference places a whole cache on the host
+ * (upload_cache, kvf_host.h:149-195). */
+cudaError_t kvf_b200_append(const kvf_args *a, int fmt, int d, int ord, int paged, const float *k_new,
+                            const float *v_new, int t_new, const int *pos, cudaStream_t stream);
 
 /* Bytes of device scratch behind kvf_b200_decode_noalloc (8 MiB). */
 #define KVF_B200_NOALLOC_SCRATCH_BYTES (8u << 20)

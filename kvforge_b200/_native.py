@@ -98,6 +98,8 @@ SIGNATURES = [
     ("kvf_b200_describe_path", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_int, c_char_p, c_int]),
     ("kvf_b200_device_errors", c_uint, []),
     ("kvf_b200_quantize", c_int, [c_int, c_int, c_int, c_void_p, c_longlong, c_void_p, c_void_p, c_void_p]),
+    ("kvf_b200_append", c_int, [ctypes.POINTER(KvfArgs), c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
+                                 c_void_p, c_void_p]),
     ("kvf_b200_version", c_char_p, []),
 ]
 

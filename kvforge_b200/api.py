@@ -192,6 +192,49 @@ def make_args(q: torch.Tensor, cache: KVCache, out: torch.Tensor, ws: Workspace)
     return a
 
 
+def append(cache: KVCache, k_new: torch.Tensor, v_new: torch.Tensor, pos: Optional[torch.Tensor] = None,
+           stream=None) -> None:
+    """Appends t_new tokens to every sequence of `cache` on its device
+    (kvf_b200_append): k_new, v_new float32 [B][Hkv][t_new][D] are quantized
+    exactly as quantize() does and written at the physical rows of tokens
+    pos[b] .. pos[b] + t_new - 1. pos (int32 [B], on the cache's device)
+    defaults to cache.seq_lens, which is then raised by t_new; a given pos
+    leaves seq_lens alone. For a paged cache the block table must already map
+    the blocks the new tokens fall in. Tokens at or past cache.n are skipped
+    and reported by device_errors() (bit 2)."""
+    if k_new.shape != v_new.shape or k_new.dim() != 4:
+        raise ValueError("k_new and v_new must both be [B][Hkv][t_new][D]")
+    B, Hkv, t_new, d = k_new.shape
+    if (B, Hkv, d) != (cache.B, cache.Hkv, cache.d):
+        raise ValueError(f"new rows {tuple(k_new.shape)} do not match the cache (B={cache.B}, Hkv={cache.Hkv}, "
+                         f"D={cache.d})")
+    if k_new.dtype != torch.float32 or v_new.dtype != torch.float32:
+        raise ValueError("k_new and v_new must be float32")
+    bump = pos is None
+    if bump:
+        if cache.seq_lens is None:
+            raise ValueError("pos is required for a cache without seq_lens")
+        pos = cache.seq_lens
+    if pos.dtype != torch.int32 or pos.numel() != B or pos.device != cache.k.device:
+        raise ValueError("pos must be an int32 tensor of B entries on the cache's device")
+    k2, v2, pos = k_new.contiguous(), v_new.contiguous(), pos.contiguous()
+    a = KvfArgs()
+    a.k = cache.k.data_ptr()
+    a.v = cache.v.data_ptr()
+    a.k_meta = cache.k_meta.data_ptr() if cache.k_meta is not None else None
+    a.v_meta = cache.v_meta.data_ptr() if cache.v_meta is not None else None
+    a.block_table = cache.block_table.data_ptr() if cache.block_table is not None else None
+    a.B, a.H, a.Hkv, a.n = B, Hkv, Hkv, cache.n
+    a.group_shift = int(round(math.log2(cache.group))) if cache.fmt != FMT_F16 else 0
+    a.block_shift = int(round(math.log2(cache.place.block_tokens))) if cache.place.paged else 0
+    a.max_blocks = cache.max_blocks
+    check("kvf_b200_append",
+          lib().kvf_b200_append(ctypes.byref(a), cache.fmt, d, cache.place.order, int(cache.place.paged),
+                                k2.data_ptr(), v2.data_ptr(), t_new, pos.data_ptr(), _stream(stream)))
+    if bump:
+        cache.seq_lens.add_(t_new)
+
+
 PATHS = {"auto": 0, "mma": 1, "tc": 2}  # KVF_PATH_AUTO / KVF_PATH_MMA / KVF_PATH_TC
 # Scheduling flags (KVF_FLAG_*), OR'ed into the path value: how the mma.sync
 # launch merges its splits and whether it balances ragged batches; the output
@@ -353,5 +396,5 @@ def device_errors() -> int:
 
 
 __all__ = ["KVCache", "Workspace", "Decoder", "decode", "PATHS", "FLAG_MERGE_KERNEL", "FLAG_GRID_MERGE",
-           "FLAG_NO_BALANCE", "merge_states", "quantize", "suggest_splits", "make_args", "describe",
+           "FLAG_NO_BALANCE", "merge_states", "quantize", "append", "suggest_splits", "make_args", "describe",
            "device_errors", "row_bytes", "groups_per_row", "scale_log2", "FMT_F16", "FMT_INT8", "FMT_INT4"]

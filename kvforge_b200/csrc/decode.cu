@@ -1052,6 +1052,10 @@ extern "C" int kvf_b200_suggest_splits_ragged(int B, int H, int Hkv, int n, int 
   return suggest_splits(B, H, Hkv, n, fmt, d, group, paged, block_tokens, true);
 }
 
+namespace kvfb {
+unsigned take_append_errors();  // quantize.cu
+}
+
 extern "C" unsigned kvf_b200_device_errors(void) {
   unsigned v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g_kvfb_error, sizeof(v)) != cudaSuccess) {
@@ -1059,6 +1063,7 @@ extern "C" unsigned kvf_b200_device_errors(void) {
     return 0xFFFFFFFFu;
   }
   if (v) cudaMemcpyToSymbol(g_kvfb_error, &zero, sizeof(zero));
+  if (kvfb::take_append_errors()) v |= 4u;  // an appended row fell outside the cache
   return v;
 }
 

@@ -144,6 +144,30 @@ def test_suggest_splits_without_gpu():
     assert l.kvf_b200_suggest_splits(0, 8, 8, 100, 0, 64, 0, 0, 0) == 1
 
 
+def test_append_argument_checks_need_no_gpu():
+    """kvf_b200_append rejects what it cannot place before touching the
+    device: a missing cache or new rows, an unknown format, order or head
+    dimension, a quantized cache without metadata, a paged cache without a
+    block table; nothing to append (t_new = 0 or B = 0) is a no-op."""
+    l = lib()
+    a = KvfArgs()
+    a.B, a.H, a.Hkv, a.n = 2, 8, 8, 64
+    fake = 0x1000  # never dereferenced: every case fails or returns before a launch
+    assert l.kvf_b200_append(None, 0, 128, 0, 0, fake, fake, 1, fake, None) == 1
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 0, 0, fake, fake, 0, fake, None) == 0  # t_new = 0
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 96, 0, 0, fake, fake, 1, fake, None) == 1   # head dim
+    assert l.kvf_b200_append(ctypes.byref(a), 3, 128, 0, 0, fake, fake, 1, fake, None) == 1  # format
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 2, 0, fake, fake, 1, fake, None) == 1  # order
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 0, 0, fake, fake, -1, fake, None) == 1  # t_new < 0
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 0, 0, None, fake, 1, fake, None) == 1  # no K rows
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 0, 0, fake, fake, 1, None, None) == 1  # no positions
+    a.k = a.v = fake
+    assert l.kvf_b200_append(ctypes.byref(a), 1, 128, 0, 0, fake, fake, 1, fake, None) == 1  # int8, no metadata
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 0, 1, fake, fake, 1, fake, None) == 1  # paged, no table
+    a.B = 0
+    assert l.kvf_b200_append(ctypes.byref(a), 0, 128, 0, 0, fake, fake, 1, fake, None) == 0  # empty batch
+
+
 def test_kernel_path_errors_need_no_gpu():
     """An explicit path is checked before anything launches: tcgen05 for a
     format it does not take is cudaErrorNotSupported, an unknown path
