@@ -131,3 +131,52 @@ def test_two_nccl_ranks_match_one_gpu():
         for exchange, got in a.items():
             assert np.abs(got - ref_a).max() < 1e-5, (r, exchange)
         assert np.abs(b - ref_b).max() < 1e-6, r
+
+
+@pytest.mark.gpu
+def test_exchange_wait_runs_out_and_reports(cuda):
+    """Failure detection without a fault: a two-rank exchange on one GPU
+    whose other rank never exists. This rank's part goes into its own cells
+    and into a stand-in buffer; the other rank's cells in its own buffer never
+    carry the step's epoch, so every bounded wait (5 ms) runs out. The kernel
+    returns, the output is zero, bit 1 of kvf_b200_device_errors() is set, and
+    the next decode on the same context is correct."""
+    import ctypes
+
+    from kvforge_b200.sharding import KvfExchange
+
+    rs = np.random.RandomState(41)
+    B, H, Hkv, n, d, splits = 1, 8, 2, 512, 128, 4
+    q = rs.standard_normal((B, H, d)).astype(np.float32)
+    K = rs.standard_normal((B, Hkv, n, d)).astype(np.float32)
+    V = rs.standard_normal((B, Hkv, n, d)).astype(np.float32)
+    place = Placement(ORD_HEAD, False, 0)
+    cache = api.KVCache.from_logical(torch.as_tensor(K, device=cuda), torch.as_tensor(V, device=cuda),
+                                     fmt=FMT_INT8, group=64, place=place)
+    qd = torch.as_tensor(q, device=cuda)
+    out = torch.full((B, H, d), 7.0, device=cuda)
+    ws = api.Workspace.allocate(B, H, d, splits, cuda, fused=False)
+    a = api.make_args(qd, cache, out, ws)
+    cells = 2 * 2 * B * H * (d + 1)
+    own = torch.zeros(cells, dtype=torch.int64, device=cuda)
+    stand_in = torch.zeros(cells, dtype=torch.int64, device=cuda)
+    x = KvfExchange()
+    x.P, x.rank, x.epoch, x.timeout_ms = 2, 0, 1, 5
+    x.gather = own.data_ptr()
+    x.peer_gather[0] = own.data_ptr()
+    x.peer_gather[1] = stand_in.data_ptr()
+    assert api.device_errors() == 0
+    rc = lib().kvf_b200_decode_exchange(ctypes.byref(a), FMT_INT8, d, 1, ORD_HEAD, 0, ctypes.byref(x), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert api.device_errors() & 2
+    assert float(out.abs().max()) == 0.0
+    # This rank's part reached both buffers, tagged with the epoch.
+    assert int((stand_in >> 32).max()) == 1 and int((own >> 32).max()) == 1
+    # The context is still usable.
+    got = api.decode(qd, cache, splits=splits).cpu().numpy()
+    _, _, kq = O.quantize(FMT_INT8, d, 64, K.reshape(-1, d))
+    _, _, vq = O.quantize(FMT_INT8, d, 64, V.reshape(-1, d))
+    ref = O.attention(q, kq.reshape(K.shape), vq.reshape(V.shape), O.scale_f32(d))
+    assert np.abs(got - ref).max() < 2e-3
+    assert api.device_errors() == 0
