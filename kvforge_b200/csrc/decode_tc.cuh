@@ -508,7 +508,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       tc::wait_ld();
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_sfree + 8u * j);
+      ptx::mbar_arrive_if(bar_sfree + 8u * j, lane == 0);
 
       // Metadata of this thread's token (rows past the chunk end hold stale
       // words and are masked).
@@ -579,10 +579,10 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
           mine = (int)u >= 0 ? (u | 0x80000000u) : ~u;
         }
       }
-      if (lane <= HT)
-        atomicMax(&ms.redx[j][half][lane], ((unsigned long long)(i + 1) << 32) | mine);
+      ptx::atom_max_u64_if(ptx::smem_u32(&ms.redx[j][half][min(lane, HT)]),
+                           ((unsigned long long)(i + 1) << 32) | mine, lane <= HT);
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_red + 8u * (2 * j + half));
+      ptx::mbar_arrive_if(bar_red + 8u * (2 * j + half), lane == 0);
 
       // ---- while the other warps of the half deliver their maxima: fold the
       // previous stage's value product. After it the value accumulator in
@@ -672,7 +672,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_pready);
+      ptx::mbar_arrive_if(bar_pready, lane == 0);
 
 #pragma unroll
       for (int e = 0; e < HT; ++e) aoprev[e] = aocur[e];

@@ -45,6 +45,25 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// mbar_arrive by the threads for which `pred` holds, as one predicated
+// instruction (no branch around it).
+__device__ __forceinline__ void mbar_arrive_if(uint32_t bar, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "@p mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n\t}" ::"r"(bar),
+      "r"((uint32_t)pred)
+      : "memory");
+}
+
+// 64-bit shared-memory atomic maximum by the threads for which `pred` holds.
+__device__ __forceinline__ void atom_max_u64_if(uint32_t addr, unsigned long long v, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+      "@p red.shared.max.u64 [%0], %1;\n\t}" ::"r"(addr),
+      "l"(v), "r"((uint32_t)pred)
+      : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
