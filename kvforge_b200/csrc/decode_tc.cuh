@@ -315,20 +315,19 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         break;
       }
       const uint32_t sk = sbase + s * p.stage_bytes;
-      if (lane == 0) ptx::mbar_arrive_expect_tx(bar_full + 8u * s, TB * 128u);
+      ptx::mbar_arrive_expect_tx_if(bar_full + 8u * s, TB * 128u, lane == 0);
       __syncwarp();
-      if (lane < p.npg)  // lane j issues box j of the tile
-        ptx::tma_g2s_4d(sk + (uint32_t)pw * (TB * 128u) + (uint32_t)lane * (uint32_t)(p.tbox * 128), tmap, 0,
-                        c1, h, c3, bar_full + 8u * s, pol);
+      // lane j issues box j of the tile
+      ptx::tma_g2s_4d_if(sk + (uint32_t)pw * (TB * 128u) + (uint32_t)lane * (uint32_t)(p.tbox * 128), tmap, 0, c1,
+                         h, c3, bar_full + 8u * s, pol, lane < p.npg);
       const uint32_t smeta = sk + 2u * TB * 128u + (uint32_t)pw * p.meta_bytes;
 #pragma unroll
       for (int k = 0; k < TB / 32; ++k) {
-        if (!msrc[k]) continue;
         const uint32_t dst = smeta + (uint32_t)((lane + 32 * k) * GPR * 4);
         if (GPR == 1)
-          ptx::cp_async_4(dst, msrc[k]);
+          ptx::cp_async_4_if(dst, msrc[k], msrc[k] != nullptr);
         else
-          ptx::cp_async_8(dst, msrc[k]);
+          ptx::cp_async_8_if(dst, msrc[k], msrc[k] != nullptr);
       }
       ptx::cp_async_arrive(bar_full + 8u * s);
       if (lane == 0) *reinterpret_cast<volatile int *>(&ms.slot_last[s]) = i;

@@ -149,6 +149,17 @@ __device__ __forceinline__ void tma_g2s_4d(uint32_t dst, const void *tmap, int c
       : "memory");
 }
 
+// tma_g2s_4d by the threads for which `pred` holds (one predicated instruction).
+__device__ __forceinline__ void tma_g2s_4d_if(uint32_t dst, const void *tmap, int c0, int c1, int c2, int c3,
+                                              uint32_t bar, uint64_t policy, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %8, 0;\n\t"
+      "@p cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;\n\t}" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy), "r"((uint32_t)pred)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -163,6 +174,25 @@ __device__ __forceinline__ void cp_async_8(uint32_t dst, const void *src) {
 }
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// cp_async_4 / cp_async_8 by the threads for which `pred` holds.
+__device__ __forceinline__ void cp_async_4_if(uint32_t dst, const void *src, bool pred) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p cp.async.ca.shared.global [%0], [%1], 4;\n\t}"
+               ::"r"(dst), "l"(src), "r"((uint32_t)pred)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_8_if(uint32_t dst, const void *src, bool pred) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p cp.async.ca.shared.global [%0], [%1], 8;\n\t}"
+               ::"r"(dst), "l"(src), "r"((uint32_t)pred)
+               : "memory");
+}
+// mbar_arrive_expect_tx by the threads for which `pred` holds.
+__device__ __forceinline__ void mbar_arrive_expect_tx_if(uint32_t bar, uint32_t bytes, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+      "@p mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(bar),
+      "r"(bytes), "r"((uint32_t)pred)
+      : "memory");
 }
 // Arrives on `bar` when every cp.async this thread issued so far completes.
 // The arrival is counted against the barrier's expected count.
