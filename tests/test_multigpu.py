@@ -6,8 +6,8 @@
 * with two or more GPUs, two ranks run the split-KV protocol (exchange fused
   into the split merge, separate NVLink push/merge kernels, NCCL all-gather;
   several steps each) and the KV-head protocol end
-  to end and must match a single-GPU decode of the same inputs (skipped on a
-  one-GPU box).
+  to end and must match a single-GPU decode of the same inputs and the fp64
+  oracle (skipped on a one-GPU box).
 """
 from __future__ import annotations
 
@@ -125,12 +125,25 @@ def test_two_nccl_ranks_match_one_gpu():
     q, K, V = _inputs(dev, "kvheads")
     ref_b = api.decode(q, api.KVCache.from_logical(K, V, fmt=FMT_INT8, group=64,
                                                    place=Placement(ORD_TOKEN, True, 16))).cpu().numpy()
+    # and the fp64 oracle over the oracle quantizer's dequantised K and V
+    orc = {}
+    for kind, fmt, group, lens in (("splitkv", FMT_INT4, 32, np.array([4321], dtype=np.int32)),
+                                   ("kvheads", FMT_INT8, 64, None)):
+        q, K, V = (t.cpu().numpy() for t in _inputs(dev, kind))
+        D = q.shape[2]
+        _, _, kd = O.quantize(fmt, D, group, K.reshape(-1, D))
+        _, _, vd = O.quantize(fmt, D, group, V.reshape(-1, D))
+        orc[kind] = O.attention(q, kd.reshape(K.shape), vd.reshape(V.shape), O.scale_f32(D), seq_lens=lens)
+    assert_close(ref_a, orc["splitkv"], "one-GPU split-KV inputs")
+    assert_close(ref_b, orc["kvheads"], "one-GPU KV-head inputs")
     for r in range(world):
         a, b, errs = res[r]
         assert errs == 0
         for exchange, got in a.items():
             assert np.abs(got - ref_a).max() < 1e-5, (r, exchange)
+            assert_close(got, orc["splitkv"], f"rank {r} split-KV, {exchange} exchange")
         assert np.abs(b - ref_b).max() < 1e-6, r
+        assert_close(b, orc["kvheads"], f"rank {r} KV heads")
 
 
 @pytest.mark.gpu
