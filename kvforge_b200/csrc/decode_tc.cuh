@@ -290,7 +290,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
         const int from_nxt = __shfl_sync(0xffffffffu, pg_nxt, idx & 31);
         lanepage = idx < 32 ? from_cur : from_nxt;
       }
-      // Metadata rows of tokens lane + 32k of the stage (null past the chunk).
+      // Metadata rows of tokens lane + 32k of the stage (null past the chunk,
+      // where the row is zero-filled instead).
       const uint32_t *msrc[TB / 32];
 #pragma unroll
       for (int k = 0; k < TB / 32; ++k) {
@@ -324,10 +325,11 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
 #pragma unroll
       for (int k = 0; k < TB / 32; ++k) {
         const uint32_t dst = smeta + (uint32_t)((lane + 32 * k) * GPR * 4);
+        const bool live = msrc[k] != nullptr;
         if (GPR == 1)
-          ptx::cp_async_4_if(dst, msrc[k], msrc[k] != nullptr);
+          ptx::cp_async_4_zfill(dst, live ? msrc[k] : meta, live ? 4u : 0u);
         else
-          ptx::cp_async_8_if(dst, msrc[k], msrc[k] != nullptr);
+          ptx::cp_async_8_zfill(dst, live ? msrc[k] : meta, live ? 8u : 0u);
       }
       ptx::cp_async_arrive(bar_full + 8u * s);
       if (lane == 0) *reinterpret_cast<volatile int *>(&ms.slot_last[s]) = i;
@@ -434,6 +436,7 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       for (int g = 0; g < GPR; ++g) qsum[e][g] = ms.qsum[half * HT + e][g];
     }
     int ev_run = 22;
+    float finv_run = exp2i(-22);
     bool ok = true;
 
     // Loads this half's CH columns of each group from tensor memory.
@@ -509,8 +512,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       __syncwarp();
       ptx::mbar_arrive_if(bar_sfree + 8u * j, lane == 0);
 
-      // Metadata of this thread's token (rows past the chunk end hold stale
-      // words and are masked).
+      // Metadata of this thread's token (rows past the chunk end were
+      // zero-filled by the producers: zero scales and zero points).
       const uint32_t smk = sbase + (uint32_t)s * p.stage_bytes + 2u * TB * 128u;
       const uint32_t smv = smk + p.meta_bytes;
       uint32_t kw[GPR], vw[GPR];
@@ -520,10 +523,6 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       } else {
         asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(kw[0]), "=r"(kw[GPR - 1]) : "r"(smk + 8u * row));
         asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(vw[0]), "=r"(vw[GPR - 1]) : "r"(smv + 8u * row));
-      }
-#pragma unroll
-      for (int g = 0; g < GPR; ++g) {
-        if (!valid) kw[g] = vw[g] = 0u;
       }
       float ks[GPR], kz[GPR], vs[GPR], vz[GPR];
       uint32_t vbits = 0;
@@ -538,10 +537,14 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       }
       float sc[HT];
       float red[HT];
+      // A row past the chunk end has zero scales, so its code term is 0; its
+      // zero-point sum starts at -inf instead of 0, so its score is -inf
+      // (valid rows: the same arithmetic as a sum started at 0).
+      const float bias = valid ? 0.f : -INFINITY;
       // Heads in pairs (packed f32x2 arithmetic).
 #pragma unroll
       for (int e = 0; e < HT; e += 2) {
-        float2 acc = make_float2(0.f, 0.f), zq = make_float2(0.f, 0.f);
+        float2 acc = make_float2(0.f, 0.f), zq = make_float2(bias, bias);
 #pragma unroll
         for (int g = 0; g < GPR; ++g) {
           const uint32_t *c = sr + g * CH;
@@ -554,8 +557,8 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
           zq = fma2(make_float2(kz[g], kz[g]), make_float2(qsum[e][g], qsum[e + 1][g]), zq);
         }
         const float2 s2 = fma2(acc, make_float2(qinv[e], qinv[e + 1]), zq);
-        sc[e] = valid ? s2.x : -INFINITY;
-        sc[e + 1] = valid ? s2.y : -INFINITY;
+        sc[e] = s2.x;
+        sc[e + 1] = s2.y;
         red[e] = sc[e];
         red[e + 1] = sc[e + 1];
       }
@@ -568,16 +571,17 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       // >= 0, all bits flipped for < 0). A warp writes stage i + 2 only after
       // all four warps of its half arrived for stage i + 1, i.e. after they
       // read stage i.
-      uint32_t mine = __reduce_max_sync(0xffffffffu, vbits);
+      const uint32_t vbmax = __reduce_max_sync(0xffffffffu, vbits);
+      float vsel = 0.f;
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
         float v;
         asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(v) : "f"(red[e]));
-        if (lane == e) {
-          const uint32_t u = __float_as_uint(v);
-          mine = (int)u >= 0 ? (u | 0x80000000u) : ~u;
-        }
+        vsel = (e == 0 || lane == e) ? v : vsel;
       }
+      // the map: u | 2^31 for u >= 0, ~u for u < 0
+      const uint32_t us = __float_as_uint(vsel);
+      const uint32_t mine = lane < HT ? us ^ ((uint32_t)((int)us >> 31) | 0x80000000u) : vbmax;
       ptx::atom_max_u64_if(ptx::smem_u32(&ms.redx[j][half][min(lane, HT)]),
                            ((unsigned long long)(i + 1) << 32) | mine, lane <= HT);
       __syncwarp();
@@ -600,15 +604,22 @@ decode_tc_kernel(const kvf_args a, const TcPlan p, const __grid_constant__ CUten
       // Head and V-scale maxima over the four warps of this half (all tokens).
 #pragma unroll
       for (int e = 0; e < HT; ++e) {
+        // the inverse map: u & ~2^31 for u >= 2^31, ~u below
         const uint32_t u = (uint32_t)ms.redx[j][half][e];
-        red[e] = __uint_as_float((int)u < 0 ? (u & 0x7FFFFFFFu) : ~u);
+        red[e] = __uint_as_float(u ^ (~(uint32_t)((int)u >> 31) | 0x80000000u));
       }
       const uint32_t vmax = (uint32_t)ms.redx[j][half][HT];
 
       // ---- online softmax, one rescale per stage; P' as 23-bit integers
-      const int ev = max(min(norm_exp(__half2float(__ushort_as_half((unsigned short)vmax)), 23), 100), -100);
-      const float fv = ev >= 0 ? exp2i(min(ev, 127)) : exp2i(max(ev, -126));
-      const float fratio = exp2i(max(min(ev - ev_run, 127), -126));
+      // ev = 23 - ceil(log2 vmax) (23 for a zero scale), within [-100, 100];
+      // the scale is a positive fp16 or zero, exactly a normal float here.
+      const uint32_t vu = __float_as_uint(__half2float(__ushort_as_half((unsigned short)vmax)));
+      const int ev = vu == 0u ? 23 : max(min(150 - (int)(vu >> 23) - ((vu & 0x7FFFFFu) != 0u), 100), -100);
+      const float fv = exp2i(ev);
+      // 2^(ev - ev_run) as a product of two powers of two: exact while
+      // |ev - ev_run| <= 126 (always, for scales within 2^100 of each other)
+      const float fratio = fv * finv_run;
+      finv_run = exp2i(-ev);
       ev_run = ev;
       // A masked row has zero scales (its metadata words were zeroed) and a
       // score of -inf, so p = 0 and every product below is 0 without a test;

@@ -186,6 +186,15 @@ __device__ __forceinline__ void cp_async_8_if(uint32_t dst, const void *src, boo
                ::"r"(dst), "l"(src), "r"((uint32_t)pred)
                : "memory");
 }
+// 8-byte cp.async that copies `bytes` (8 or 0) from src and zero-fills the
+// rest: with 0 nothing is read (src must still be a valid address) and the
+// destination is zeroed, completing through the same cp.async tracking.
+__device__ __forceinline__ void cp_async_8_zfill(uint32_t dst, const void *src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_4_zfill(uint32_t dst, const void *src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
 // mbar_arrive_expect_tx by the threads for which `pred` holds.
 __device__ __forceinline__ void mbar_arrive_expect_tx_if(uint32_t bar, uint32_t bytes, bool pred) {
   asm volatile(
