@@ -482,6 +482,35 @@ def test_decoder_graph_replays_match_direct_decode(cuda, fmt, group, place, zero
     assert api.device_errors() == 0
 
 
+@pytest.mark.parametrize("zero_copy", [True, False], ids=["zero_copy", "copies"])
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+def test_decoder_graph_on_each_int8_kernel(cuda, zero_copy, kernel):
+    """The same with 32 KV-head units (the tcgen05 kernel's range) on each
+    int8 kernel: the staged queries and the output in pinned host memory
+    equal api.decode on the same path bit for bit, and the oracle."""
+    rs = np.random.RandomState(37)
+    B, H, Hkv, D, n = 8, 32, 4, 128, 700
+    K = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    V = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    lens = np.array([700, 1, 333, 0, 512, 699, 128, 129], dtype=np.int32)
+    cache = api.KVCache.from_logical(K, V, fmt=FMT_INT8, group=64, place=Placement(ORD_TOKEN, True, 16),
+                                     seq_lens=lens)
+    dec = api.Decoder(cache, H, splits=3, zero_copy=zero_copy, path=kernel)
+    assert f"kernel={'tcgen05' if kernel == 'tc' else 'mma.sync'}" in api.describe(
+        dec.q, cache, dec.workspace, path=kernel)
+    Kn, Vn = K.cpu().numpy(), V.cpu().numpy()
+    _, _, kq = O.quantize(FMT_INT8, D, 64, Kn.reshape(-1, D))
+    _, _, vq = O.quantize(FMT_INT8, D, 64, Vn.reshape(-1, D))
+    for step in range(3):
+        q = torch.as_tensor(rs.standard_normal((B, H, D)).astype(np.float32))
+        got = dec.step(q).clone()
+        want = api.decode(q.to(cuda), cache, splits=3, path=kernel).cpu()
+        assert torch.equal(got, want), step
+        ref = O.attention(q.numpy(), kq.reshape(Kn.shape), vq.reshape(Vn.shape), O.scale_f32(D), seq_lens=lens)
+        assert_close(got.numpy(), ref, f"decoder {kernel} step {step}")
+    assert api.device_errors() == 0
+
+
 def test_decode_from_host_rejects_pageable_buffers(cuda):
     """Host buffers the device cannot address are refused before any launch."""
     rs = np.random.RandomState(32)
