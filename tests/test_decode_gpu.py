@@ -511,6 +511,61 @@ def test_decoder_graph_on_each_int8_kernel(cuda, zero_copy, kernel):
     assert api.device_errors() == 0
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["in_kernel_merge", "merge_kernel"])
+@pytest.mark.parametrize("place", [Placement(ORD_TOKEN, True, 16), Placement(ORD_HEAD, False, 0)],
+                         ids=lambda p: p.name)
+def test_decode_from_host_on_the_tcgen05_path(cuda, fused, place):
+    """kvf_b200_decode_from_host on the tcgen05 path with more blocks than one
+    wave (12 sequences x 8 KV heads x 40 splits), ragged lengths, output to
+    pinned host memory and lse on the device: equal to api.decode bit for
+    bit, directly and in a captured graph, with either merge."""
+    rs = np.random.RandomState(43)
+    B, H, Hkv, D, n, S = 12, 64, 8, 128, 300, 40
+    K = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    V = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
+    lens = rs.randint(0, n + 1, B).astype(np.int32)
+    lens[0] = n
+    cache = api.KVCache.from_logical(K, V, fmt=FMT_INT8, group=64, place=place, seq_lens=lens)
+    q = rs.standard_normal((B, H, D)).astype(np.float32)
+    qd = torch.as_tensor(q, device=cuda)
+    want_out = torch.empty_like(qd)
+    want_lse = torch.empty((B, H), device=cuda)
+    api.decode(qd, cache, out=want_out, lse=want_lse, splits=S, path="tc",
+               workspace=api.Workspace.allocate(B, H, D, S, cuda, fused=fused))
+    q_host = torch.as_tensor(q).pin_memory()
+    out_host = torch.full((B, H, D), float("nan")).pin_memory()
+    lse = torch.full((B, H), float("nan"), device=cuda)
+    ws = api.Workspace.allocate(B, H, D, S, cuda, fused=fused)
+    qbuf = torch.zeros_like(qd)
+    a = api.make_args(qbuf, cache, want_out, ws)
+    a.out = out_host.data_ptr()
+    a.lse = lse.data_ptr()
+    g = H // Hkv
+
+    def issue():  # on the current stream (the capture stream inside the graph)
+        check("kvf_b200_decode_from_host",
+              lib().kvf_b200_decode_from_host(ctypes.byref(a), FMT_INT8, D, g, place.order, int(place.paged),
+                                              api.PATHS["tc"], ctypes.c_void_p(q_host.data_ptr()),
+                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+    issue()
+    torch.cuda.synchronize()
+    assert torch.equal(out_host, want_out.cpu())
+    assert torch.equal(lse, want_lse)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        issue()
+    out_host.fill_(float("nan"))
+    lse.fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out_host, want_out.cpu())
+    assert torch.equal(lse, want_lse)
+    if fused:
+        assert int(ws.split_sem.abs().sum()) == 0
+    assert api.device_errors() == 0
+
+
 def test_decode_from_host_rejects_pageable_buffers(cuda):
     """Host buffers the device cannot address are refused before any launch."""
     rs = np.random.RandomState(32)
