@@ -158,7 +158,12 @@ cudaError_t kvf_b200_decode_path(const kvf_args *a, int fmt, int d, int g, int o
  * takes it) is launched
  * as its programmatic dependent, so the K/V stream starts while the queries
  * are still in flight; the decode reads them only once the copy kernel has
- * completed. a->out (and a->lse) may likewise point at such host memory: the
+ * completed. On the tcgen05 path, when the grid is more than one wave and the
+ * other sequences' queries are 256 KB or more, the sequences whose blocks fit
+ * one wave are copied and decoded first, and the rest are copied by a narrow
+ * kernel running beside that decode and decoded after it (four launches on
+ * `stream`, each the programmatic dependent of the one before; the output is
+ * the same bit for bit). a->out (and a->lse) may likewise point at such host memory: the
  * kernels then write the result there directly. Host buffers the device cannot
  * address (pageable memory) are rejected with cudaErrorInvalidValue before
  * anything launches. Otherwise as kvf_b200_decode_path. */

@@ -836,6 +836,76 @@ bool device_addressable(const void *p) {
   return at.type == cudaMemoryTypeHost && at.devicePointer == p;
 }
 
+// Copies n4 float4 from host memory with 128-thread blocks of at most 32
+// registers a thread, so that one block fits beside two resident tcgen05
+// decode blocks on an SM (they leave 4096 registers); each thread keeps
+// several loads in flight. Launched as the programmatic dependent of a decode
+// grid whose data it does not touch, it starts at once and lets its own
+// dependent launch.
+__global__ void __launch_bounds__(128, 16) stage_in_narrow_kernel(float4 *dst, const float4 *src, int n4) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int stride = gridDim.x * blockDim.x;
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n4; i += 4 * stride) {
+    const float4 v0 = src[i], v1 = src[i + stride], v2 = src[i + 2 * stride], v3 = src[i + 3 * stride];
+    dst[i] = v0;
+    dst[i + stride] = v1;
+    dst[i + 2 * stride] = v2;
+    dst[i + 3 * stride] = v3;
+  }
+  for (; i < n4; i += stride) dst[i] = src[i];
+}
+
+// Arguments of sequences [b0, b0 + nb) of a batch.
+kvf_args sub_batch(const kvf_args *a, const Shape &sh, int d, int b0, int nb) {
+  kvf_args s = *a;
+  const long long qo = (long long)b0 * a->H * d;
+  s.q = a->q + qo;
+  s.out = a->out + qo;
+  if (a->lse) s.lse = a->lse + (long long)b0 * a->H;
+  if (a->seq_lens) s.seq_lens = a->seq_lens + b0;
+  if (a->part_o) s.part_o = a->part_o + (long long)b0 * a->H * a->splits * d;
+  if (a->part_ml) s.part_ml = a->part_ml + (long long)b0 * a->H * a->splits * 2;
+  if (a->split_sem) s.split_sem = a->split_sem + 2LL * b0 * a->Hkv;  // two words per (sequence, KV head)
+  if (sh.paged) {
+    s.block_table = a->block_table + (long long)b0 * a->max_blocks;
+  } else {
+    const long long rows = (long long)b0 * a->n * a->Hkv;  // a sequence's rows are contiguous in both orders
+    s.k = a->k + rows * row_bytes(sh.fmt, sh.d);
+    s.v = a->v + rows * row_bytes(sh.fmt, sh.d);
+    if (sh.gpr > 0) {
+      s.k_meta = static_cast<const uint32_t *>(a->k_meta) + rows * sh.gpr;
+      s.v_meta = static_cast<const uint32_t *>(a->v_meta) + rows * sh.gpr;
+    }
+  }
+  s.B = nb;
+  return s;
+}
+
+// Host-query steps of large batches on the tcgen05 path. With one staging
+// kernel for the whole batch every decode block waits for all of the queries
+// (config 5: 2 MB, ~40 us over PCIe). Instead the sequences whose blocks fit
+// one wave are staged and decoded first; the rest are staged by a narrow copy
+// kernel that runs beside that decode, and decoded after it, each launch the
+// programmatic dependent of the one before. Returns the number of sequences
+// of the first part, B for no split (one wave holds everything, or the rest
+// of the queries is small).
+constexpr long long kSplitStageMinBytes = 256 * 1024;
+
+int first_wave_sequences(const kvf_args *a, const Shape &sh, int d) {
+  if (a->B < 2) return a->B;
+  TcLaunch L;
+  if (plan_tc(a, sh, L) != cudaSuccess) {
+    cudaGetLastError();
+    return a->B;
+  }
+  const long long per_seq = (long long)a->Hkv * std::max(1, a->splits);
+  const long long s1 = (long long)L.occupancy * sm_count() / per_seq;  // every block of part 1 resident at once
+  if (s1 < 1 || s1 >= a->B) return a->B;
+  const long long rest = (a->B - s1) * (long long)a->H * d * 4;
+  return rest >= kSplitStageMinBytes && rest / 16 <= 0x7FFFFFFFLL ? (int)s1 : a->B;
+}
+
 } // namespace
 } // namespace kvfb
 
@@ -852,12 +922,36 @@ extern "C" cudaError_t kvf_b200_decode_from_host(const kvf_args *a, int fmt, int
   if (!device_addressable(q_host) || !device_addressable(a->q) || !device_addressable(a->out) ||
       (a->lse && !device_addressable(a->lse)))
     return cudaErrorInvalidValue;
-  const long long n4 = n / 4;
-  stage_in_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, stream>>>(
-      reinterpret_cast<float4 *>(const_cast<float *>(a->q)), reinterpret_cast<const float4 *>(q_host), n4);
+  int kernel = 1;
+  e = resolve_path(sh, a->B * a->Hkv, path, kernel);
+  if (e != cudaSuccess) return e;
+  const int s1 = kernel == 2 ? first_wave_sequences(a, sh, d) : a->B;
+  const long long h1 = (long long)s1 * a->H * d;
+  stage_in_kernel<<<(unsigned)((h1 / 4 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<float4 *>(const_cast<float *>(a->q)), reinterpret_cast<const float4 *>(q_host), h1 / 4);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return decode_impl(a, fmt, d, g, ord, paged, path, stream, nullptr, true);
+  if (s1 == a->B) return decode_impl(a, fmt, d, g, ord, paged, path, stream, nullptr, true);
+  // Both parts on the tcgen05 kernel (the launcher's unit rule would see each
+  // part's smaller batch), with the same flags.
+  const int ptc = KVF_PATH_TC | (path & ~kPathMask);
+  const kvf_args a1 = sub_batch(a, sh, d, 0, s1), a2 = sub_batch(a, sh, d, s1, a->B - s1);
+  e = decode_impl(&a1, fmt, d, g, ord, paged, ptc, stream, nullptr, true);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)sm_count());
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, stage_in_narrow_kernel, reinterpret_cast<float4 *>(const_cast<float *>(a2.q)),
+                         reinterpret_cast<const float4 *>(q_host + h1), (int)((n - h1) / 4));
+  if (e != cudaSuccess) return e;
+  return decode_impl(&a2, fmt, d, g, ord, paged, ptc, stream, nullptr, true);
 }
 
 extern "C" cudaError_t kvf_b200_decode_exchange(const kvf_args *a, int fmt, int d, int g, int ord, int paged,

@@ -516,11 +516,14 @@ def test_decoder_graph_on_each_int8_kernel(cuda, zero_copy, kernel):
                          ids=lambda p: p.name)
 def test_decode_from_host_on_the_tcgen05_path(cuda, fused, place):
     """kvf_b200_decode_from_host on the tcgen05 path with more blocks than one
-    wave (12 sequences x 8 KV heads x 40 splits), ragged lengths, output to
-    pinned host memory and lse on the device: equal to api.decode bit for
-    bit, directly and in a captured graph, with either merge."""
+    wave: 12 sequences x 8 KV heads x 12 splits, 96 blocks a sequence, so on
+    148 SMs x 2 sequences 0-2 are staged and decoded first and sequences 3-11
+    (295 KB of queries) staged beside that decode and decoded after it.
+    Ragged lengths, output to pinned host memory, lse on the device: equal to
+    api.decode bit for bit, directly and in a captured graph, with either
+    merge."""
     rs = np.random.RandomState(43)
-    B, H, Hkv, D, n, S = 12, 64, 8, 128, 300, 40
+    B, H, Hkv, D, n, S = 12, 64, 8, 128, 300, 12
     K = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
     V = torch.as_tensor(rs.standard_normal((B, Hkv, n, D)).astype(np.float32), device=cuda)
     lens = rs.randint(0, n + 1, B).astype(np.int32)
