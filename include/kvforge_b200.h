@@ -68,8 +68,8 @@ enum { KVF_ORD_HEAD = 0, KVF_ORD_TOKEN = 1 };
  *                KV head) merges (counter word 2u of unit u); on the mma.sync
  *                path, for batches with at least two merge slices per block,
  *                a cooperative launch merges after a grid barrier (words 1
- *                and 3), and for grids of one wave (int8 codes) or of one
- *                wave with at most 64 splits (int4, f16) the last
+ *                and 3), and for grids of one wave with at most 160
+ *                splits (int8, int4) or 64 (f16) the last
  *                finishers of each (sequence, head group) g share
  *                its merge (words 2g and 2g + 1). NULL = the reference's
  *                two-launch scheme. Calls sharing one array must not overlap

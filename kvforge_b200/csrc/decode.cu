@@ -664,11 +664,12 @@ bool coop_fits(void *fn, int blocks, int threads, uint32_t smem) {
 // cooperative launch costs more than the merge kernel it replaces). So by
 // default it is used from two slices per decode block; KVF_FLAG_GRID_MERGE
 // asks for it wherever possible, KVF_FLAG_MERGE_KERNEL never.
-// Split counts up to which the last finishers merge (int8 codes: any count
-// of a one-wave grid, which is at most one split per decode block; int4 and
-// f16: 64). Measured below, at the plan_mma call.
+// Split counts up to which the last finishers merge: 64 for f16; for int8
+// and int4 the most for which the tail merge's narrower loads give the merge
+// kernel's bits (kMergeWarps x kTailMergeUnroll = 160). Measured below, at
+// the plan_mma call.
 constexpr int kTailMergeMaxSplits = 64;
-constexpr int kTailMergeMaxSplitsInt8 = 1 << 20;
+constexpr int kTailMergeMaxSplitsInt = kMergeWarps * kTailMergeUnroll;
 
 bool coop_wanted(const kvf_args *a, int d, long long blocks, int flags) {
   if (a->splits <= 1 || !a->split_sem || (long long)a->B * a->Hkv < 2) return false;
@@ -714,7 +715,7 @@ cudaError_t plan_mma(const kvf_args *a, const Shape &sh, int d, const kvf_exchan
   // step in 24.2 us instead of 25.6 with the merge kernel, 147 splits (8 KV
   // heads, int8:64) in the same 27.6 us (one launch instead of two, so ~4 us
   // less host time per call), 147 splits of int4:32 in 40.9 instead of 37.9.
-  const int tail_max = sh.fmt == 1 ? kTailMergeMaxSplitsInt8 : kTailMergeMaxSplits;
+  const int tail_max = sh.fmt != 0 ? kTailMergeMaxSplitsInt : kTailMergeMaxSplits;
   L.p.tail_merge = (!x && !want_coop && a->split_sem && a->splits > 1 && a->splits <= tail_max &&
                     L.p.bal_gran == 0 && !(flags & KVF_FLAG_MERGE_KERNEL) && (long long)L.blocks <= slots)
                        ? 1

@@ -385,6 +385,11 @@ __device__ __forceinline__ int norm_exp(float m, int top) {
 // 256 splits), and the warps' partial (M, L, O) are combined the same way.
 constexpr int kMergeWarps = 8;
 constexpr int kMergeUnroll = 32;
+// The decode kernel's tail merge loads 20 splits per warp and round (fewer
+// live registers beside the decode's own); for at most kMergeWarps x 20 =
+// 160 splits both take one round, in which the extra slots of the wider one
+// add exact zeros, so the two give the same bits.
+constexpr int kTailMergeUnroll = 20;
 
 // Merged (M, L, O) of one (query head, 32-column slice) over all splits, for
 // warp 0 (lane = column); warps 0 .. nw-1 of the caller's block take part (a
@@ -395,6 +400,7 @@ struct MergeSmem {
   float o[kMergeWarps][32];
 };
 
+template <int U = kMergeUnroll>
 __device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long head, int col, bool colok,
                                              MergeSmem &sm, float &Mt, float &Lt, float &Ot, int nw = kMergeWarps,
                                              int nsp = -1) {
@@ -410,10 +416,10 @@ __device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long
 
   for (int vw = warp; vw < kMergeWarps; vw += nw) {
     float M = -INFINITY, L = 0.f, O = 0.f;
-    for (int base = vw; base < NS; base += kMergeWarps * kMergeUnroll) {
-      float ms[kMergeUnroll], ls[kMergeUnroll], os[kMergeUnroll];
+    for (int base = vw; base < NS; base += kMergeWarps * U) {
+      float ms[U], ls[U], os[U];
 #pragma unroll
-      for (int k = 0; k < kMergeUnroll; ++k) {
+      for (int k = 0; k < U; ++k) {
         const int sp = base + k * kMergeWarps;
         const bool v = sp < NS;
         ms[k] = v ? __ldcg(ml + 2 * sp) : -INFINITY;
@@ -422,13 +428,13 @@ __device__ __forceinline__ void merge_splits(const kvf_args &a, int d, long long
       }
       float mx = M;
 #pragma unroll
-      for (int k = 0; k < kMergeUnroll; ++k) mx = fmaxf(mx, ms[k]);
+      for (int k = 0; k < U; ++k) mx = fmaxf(mx, ms[k]);
       if (mx == -INFINITY) continue;
       const float r = exp2f(M - mx);  // 0 when M is -inf
       L *= r;
       O *= r;
 #pragma unroll
-      for (int k = 0; k < kMergeUnroll; ++k) {
+      for (int k = 0; k < U; ++k) {
         const float w = ms[k] == -INFINITY ? 0.f : exp2f(ms[k] - mx);
         L = fmaf(ls[k], w, L);
         O = fmaf(os[k], w, O);
@@ -1322,7 +1328,7 @@ decode_kernel(const kvf_args a, const Plan p, const __grid_constant__ CUtensorMa
         const int col = zc * 32 + lane;
         const bool colok = col < D;
         float Mt, Lt, Ot;
-        merge_splits(a, D, head, col, colok, tsm, Mt, Lt, Ot, p.hh, S);
+        merge_splits<kTailMergeUnroll>(a, D, head, col, colok, tsm, Mt, Lt, Ot, p.hh, S);
         if (warp == 0) {
           if (colok) a.out[head * D + col] = Lt > 0.f ? Ot / Lt : 0.f;
           if (lane == 0 && zc == 0 && a.lse) a.lse[head] = Lt > 0.f ? Mt + log2f(Lt) : -INFINITY;

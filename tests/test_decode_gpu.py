@@ -286,10 +286,12 @@ def test_split_count_does_not_change_the_result(cuda, kernel_path):
     (FMT_INT4, 32, Placement(ORD_HEAD, False, 0), 128, 4, 5000, 48),    # gqa int4, some splits empty
     (FMT_F16, 0, Placement(ORD_TOKEN, False, 0), 64, 2, 3000, 64),      # d=64, the most splits f16 takes
     (FMT_INT8, 64, Placement(ORD_TOKEN, False, 0), 128, 4, 20000, 147),  # int8: a whole wave, late splits empty
+    (FMT_INT4, 32, Placement(ORD_HEAD, False, 0), 128, 4, 30000, 147),   # int4: a whole wave
 ])
 def test_tail_merge_matches_the_merge_kernel(cuda, fmt, group, place, d, gq, n, splits):
     """A single sequence on the mma.sync kernel with split counters in one
-    wave (int4 and f16 with at most 64 splits): the last finishers of each head group merge
+    wave (at most 160 splits for int8 and int4, 64 for f16): the last
+    finishers of each head group merge
     the splits inside the launch. The result equals the separate merge
     kernel's bit for bit (the same merge arithmetic), matches the oracle, and
     the counters are back at zero after every call."""
