@@ -904,7 +904,8 @@ int first_wave_sequences(const kvf_args *a, const Shape &sh, int d) {
   const long long s1 = (long long)L.occupancy * sm_count() / per_seq;  // every block of part 1 resident at once
   if (s1 < 1 || s1 >= a->B) return a->B;
   const long long rest = (a->B - s1) * (long long)a->H * d * 4;
-  return rest >= kSplitStageMinBytes && rest / 16 <= 0x7FFFFFFFLL ? (int)s1 : a->B;
+  // (the narrow kernel indexes float4 with 32-bit integers, i + 3 x its grid)
+  return rest >= kSplitStageMinBytes && rest / 16 <= (1LL << 30) ? (int)s1 : a->B;
 }
 
 } // namespace
